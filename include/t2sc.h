@@ -1,0 +1,160 @@
+/* t2sc — B200 (sm_100a) sparse submanifold convolution for TRELLIS.2-Mojo.
+ *
+ * C ABI of libt2sc.so. Every entry point returns an int status (T2SC_OK = 0)
+ * and never aborts the process; t2sc_last_error() returns the message of the
+ * last failure on a context. Plain pointers and sizes only.
+ *
+ * Reference interfaces replaced (paths inside the TRELLIS.2-Mojo project):
+ *   SparseConv3d(weight [Co,Kd,Kh,Kw,Ci], bias, dilation)  trellis2_mojo/sparse/conv.mojo:31-47
+ *   SparseConv3d._neighbor_map -> (src, tgt, kidx)          trellis2_mojo/sparse/conv.mojo:56-96
+ *   CSR counting sort by target                             trellis2_mojo/sparse/conv.mojo:117-147
+ *   SparseConv3d.forward                                    trellis2_mojo/sparse/conv.mojo:98-199
+ *   GpuSparseConv.try_build / forward                       trellis2_mojo/gpu/conv.mojo:264-329, 334-477
+ *   sparse_conv3d_from (attach point at model load)         trellis2_mojo/loaders.mojo:43-50
+ *   SparseTensor coords int32 [N,4] (b,x,y,z) + spatial cache  trellis2_mojo/sparse/basic.mojo:296-339, 542-558
+ *   SparseUpsample.forward_subdivision                      trellis2_mojo/sparse/spatial/basic.mojo:144-174
+ *   SparseChannel2Spatial.forward_subdivision / _unfold     trellis2_mojo/sparse/spatial/spatial2channel.mojo:97-145
+ *   _binarize (sub > 0)                                     trellis2_mojo/models/sc_vaes/sparse_unet_vae.mojo:30-37
+ *   activation(ACT_SILU): v / (1 + exp(-v))                 trellis2_mojo/modules/nn.mojo:567-568
+ *
+ * Threading: calls on one context are serialised by the caller (as the
+ * reference's single GpuContext is); all device work of a context runs on
+ * its stream. "_device" entry points take device pointers and are
+ * asynchronous on that stream; the others take host pointers and return
+ * after the results are in host memory.
+ */
+#ifndef T2SC_H
+#define T2SC_H
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ---- */
+#define T2SC_OK 0
+#define T2SC_ERR_INVALID 1     /* bad argument or shape (reference: raise Error) */
+#define T2SC_ERR_CUDA 2        /* a CUDA runtime call failed */
+#define T2SC_ERR_OOM 3         /* device allocation failed */
+#define T2SC_ERR_RANGE 4       /* coordinate outside the packable range [-512, 1536) or batch < 0 */
+#define T2SC_ERR_TIMEOUT 5     /* a bounded device wait gave up; the context stays usable */
+#define T2SC_ERR_UNSUPPORTED 6 /* shape not supported by this build */
+#define T2SC_ERR_CAPACITY 7    /* caller's output buffer too small; required size returned */
+
+/* ---- arithmetic modes (conv weights, inputs and outputs) ---- */
+#define T2SC_DT_F32 0  /* f32 in/out, f32-accurate (split-TF32 tensor cores) */
+#define T2SC_DT_F16 1  /* f16 in/out, f32 accumulate */
+#define T2SC_DT_BF16 2 /* bf16 in/out, f32 accumulate */
+
+/* ---- epilogue flags, applied in this order after the bias ---- */
+#define T2SC_SILU 1     /* y = y / (1 + exp(-y)) */
+#define T2SC_RESIDUAL 2 /* y += residual (same dtype and shape as y) */
+
+/* ---- subdivision ---- */
+#define T2SC_SUB_NONZERO 0  /* keep child c of row r iff sub[r*8+c] != 0 (forward_subdivision) */
+#define T2SC_SUB_POSITIVE 1 /* keep iff sub[r*8+c] > 0 (_binarize then forward_subdivision) */
+#define T2SC_FEATS_NONE 0     /* coordinates only */
+#define T2SC_FEATS_UPSAMPLE 1 /* out[e] = x[parent]               (SparseUpsample) */
+#define T2SC_FEATS_C2S 2      /* out[e] = x[parent, c*C:(c+1)*C]  (SparseChannel2Spatial) */
+
+typedef struct t2sc_ctx t2sc_ctx;
+typedef struct t2sc_coords t2sc_coords;
+typedef struct t2sc_conv t2sc_conv;
+
+/* ---- context: one per device (replaces GpuContext, gpu/context.mojo:116-165) ---- */
+int t2sc_ctx_create(int device, t2sc_ctx **out);
+int t2sc_ctx_destroy(t2sc_ctx *ctx);
+/* Run this context's work on a caller-owned cudaStream_t (NULL restores the
+ * context's own stream). */
+int t2sc_ctx_set_stream(t2sc_ctx *ctx, void *cuda_stream);
+int t2sc_ctx_synchronize(t2sc_ctx *ctx);
+const char *t2sc_last_error(const t2sc_ctx *ctx);
+/* Kernel launches issued by this context since creation (diagnostics). */
+int t2sc_ctx_launch_count(const t2sc_ctx *ctx, int64_t *count);
+/* Library version string, e.g. "t2sc 0.1 sm_100a". */
+const char *t2sc_version(void);
+
+/* ---- coordinates: device copy + coordinate hash + cached neighbour maps.
+ * Equivalent of a SparseTensor's coords and its spatial cache
+ * (sparse/basic.mojo:542-558): maps are built on first use per
+ * (kernel, dilation) and reused by every conv on the same coordinates. ---- */
+int t2sc_coords_create(t2sc_ctx *ctx, const int32_t *coords_host, int64_t n, t2sc_coords **out);
+int t2sc_coords_create_device(t2sc_ctx *ctx, const int32_t *coords_dev, int64_t n, t2sc_coords **out);
+int t2sc_coords_destroy(t2sc_coords *c);
+int t2sc_coords_count(const t2sc_coords *c, int64_t *n);
+/* Build (or fetch) the neighbour map; returns the edge count E. */
+int t2sc_coords_build_map(t2sc_coords *c, int kd, int kh, int kw, int dilation, int64_t *n_edges);
+
+/* Edge lists exactly as SparseConv3d._neighbor_map returns them
+ * (conv.mojo:56-96): kernel-offset-major, target ascending. Host buffers of
+ * capacity `cap`; if E > cap, returns T2SC_ERR_CAPACITY with *n_edges = E. */
+int t2sc_neighbor_map_export(t2sc_coords *c, int kd, int kh, int kw, int dilation,
+                             int64_t *src, int64_t *tgt, int64_t *kidx, int64_t cap,
+                             int64_t *n_edges);
+/* CSR exactly as conv.mojo:117-147 builds it: row_start [N+1], src_s [E],
+ * kidx_s [E] (kernel index ascending within a row). */
+int t2sc_csr_export(t2sc_coords *c, int kd, int kh, int kw, int dilation,
+                    int64_t *row_start, int64_t *src_s, int64_t *kidx_s, int64_t cap,
+                    int64_t *n_edges);
+
+/* ---- conv: weights uploaded once (replaces GpuSparseConv.try_build,
+ * gpu/conv.mojo:264-329). weight is host f32 [Co, Kd, Kh, Kw, Ci] (the
+ * conv_none layout), bias host f32 [Co] or NULL. Unlike try_build there is
+ * no Co % 64 gate and no decline: every shape runs on the GPU. ---- */
+int t2sc_conv_create(t2sc_ctx *ctx, const float *weight, const float *bias, int co, int kd,
+                     int kh, int kw, int ci, int dilation, int dtype, t2sc_conv **out);
+int t2sc_conv_destroy(t2sc_conv *conv);
+
+/* y [N, Co] = SubMConv(x [N, Ci]) + bias, then the epilogue flags.
+ * Host f32 buffers in every dtype mode (16-bit modes round x to the mode's
+ * type on the device). residual: host f32 [N, Co] or NULL. Replaces
+ * SparseConv3d.forward (conv.mojo:98-199). */
+int t2sc_conv_forward(t2sc_conv *conv, t2sc_coords *coords, const float *x, float *y, int flags,
+                      const float *residual);
+/* Same on device buffers whose element type is the conv's dtype (f32, f16
+ * or bf16); asynchronous on the context stream. */
+int t2sc_conv_forward_device(t2sc_conv *conv, t2sc_coords *coords, const void *x, void *y,
+                             int flags, const void *residual);
+/* A chain of convs on the same coordinates with device-resident
+ * intermediates: host f32 x [N, Ci0] in, host f32 y [N, Co_last] out.
+ * flags[i] applies to layer i; T2SC_RESIDUAL on layer i adds the chain input
+ * x (the identity residual of a residual block). All convs share one dtype. */
+int t2sc_conv_chain_forward(t2sc_conv *const *convs, int n_layers, t2sc_coords *coords,
+                            const float *x, float *y, const int *flags);
+
+/* ---- subdivision (SparseUpsample / SparseChannel2Spatial
+ * forward_subdivision). Children are emitted parent-major, child index
+ * ascending; child c of parent (b,x,y,z) is (b, 2x + (c&1), 2y + ((c>>1)&1),
+ * 2z + ((c>>2)&1)). Host buffers: sub f32 [N,8]; feats f32 [N,C] for
+ * UPSAMPLE or [N,8*C] for C2S (C = output channels), NULL for NONE.
+ * Outputs sized for the worst case M = 8N: out_coords int32 [8N,4],
+ * out_feats f32 [8N,C], out_parent int64 [8N] (nullable),
+ * out_subidx int64 [8N] (nullable). *m receives M. ---- */
+int t2sc_subdivide(t2sc_ctx *ctx, const int32_t *coords, int64_t n, const float *sub, int keep_mode,
+                   const float *feats, int c, int feats_mode, int32_t *out_coords, float *out_feats,
+                   int64_t *out_parent, int64_t *out_subidx, int64_t *m);
+/* Device variant: feats/out_feats element type given by dtype; out_parent
+ * and out_subidx are int32 on the device (nullable). *m is a host pointer;
+ * the call synchronises the stream once to read it. */
+int t2sc_subdivide_device(t2sc_ctx *ctx, const int32_t *coords, int64_t n, const float *sub,
+                          int keep_mode, const void *feats, int c, int feats_mode, int dtype,
+                          int32_t *out_coords, void *out_feats, int32_t *out_parent,
+                          int32_t *out_subidx, int64_t *m);
+
+/* ---- synthetic inputs (seeded shells of the benchmark configurations) ----
+ * Active cells of a G^3 grid with | |p-c| - R(1 + 0.1 sin(3t) cos(2(f+phase))) | <= h,
+ * c = G/2, t = acos((p_z-c)/|p-c|), f = atan2(p_y-c, p_x-c), phase = 0 for
+ * seed 0 else 2*pi*u0 (u0 = first draw of the project RNG, rng.mojo:20-37).
+ * Rows lexicographic (b=batch, x, y, z). cap rows; *n receives the count. */
+int t2sc_synth_shell(int g, double radius, double half_width, uint64_t seed, int batch,
+                     int32_t *coords, int64_t cap, int64_t *n);
+/* Standard normals * std from the project RNG (xorshift64* seeded by
+ * splitmix64, Box-Muller; trellis2_mojo/rng.mojo:17-52). */
+int t2sc_synth_normal(uint64_t seed, float std, float *out, int64_t count);
+/* out[i] = 1.0 if next_f64() < p else 0.0 (seeded Bernoulli child mask). */
+int t2sc_synth_bernoulli(uint64_t seed, double p, float *out, int64_t count);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* T2SC_H */

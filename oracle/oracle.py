@@ -1,0 +1,146 @@
+"""ctypes wrapper of the CPU restatement (liboracle, t2sc_oracle.c).
+
+TEST INFRASTRUCTURE ONLY: imported by tests/, __graft_entry__.smoke() and
+bench.py's CPU-baseline leg as the checker and the timed CPU reference.
+Parity status: follows the reference source (file:line in t2sc_oracle.c);
+values are unpinned beyond code-following, edge counts are pinned to the
+reference's published dense-blob table.
+"""
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB = os.path.join(HERE, "_build", "libt2sc_oracle.so")
+
+
+def build():
+    src = [os.path.join(HERE, f) for f in ("t2sc_oracle.c", "t2sc_oracle.h", "Makefile")]
+    if not os.path.exists(LIB) or any(os.path.getmtime(s) > os.path.getmtime(LIB) for s in src):
+        subprocess.run(["make", "-s", "-C", HERE], check=True)
+    return LIB
+
+
+_lib = None
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB):
+            build()
+        L = ctypes.CDLL(LIB)
+        P, I, I64 = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64
+        L.orc_pack_key.restype = I64
+        L.orc_pack_key.argtypes = [I64, I64, I64, I64]
+        L.orc_neighbor_map.restype = I64
+        L.orc_neighbor_map.argtypes = [P, I64, I, I, I, I, P, P, P, I64]
+        L.orc_csr.restype = None
+        L.orc_csr.argtypes = [I64, I64, P, P, P, P, P, P]
+        L.orc_conv_forward.restype = None
+        L.orc_conv_forward.argtypes = [P, I64, I, P, P, I, I, P, P, P, I64, P, I]
+        L.orc_conv_forward_rows.restype = None
+        L.orc_conv_forward_rows.argtypes = [P, I64, I, P, P, I, I, P, P, P, P, I]
+        L.orc_silu.restype = None
+        L.orc_silu.argtypes = [P, I64]
+        L.orc_add.restype = None
+        L.orc_add.argtypes = [P, P, I64]
+        L.orc_round16.restype = None
+        L.orc_round16.argtypes = [P, I64, I]
+        L.orc_subdivide.restype = I64
+        L.orc_subdivide.argtypes = [P, I64, P, I, P, P, P]
+        L.orc_select_rows.restype = None
+        L.orc_select_rows.argtypes = [P, I, P, I64, P]
+        L.orc_c2s_unfold.restype = None
+        L.orc_c2s_unfold.argtypes = [P, I, P, P, I64, P]
+        _lib = L
+    return _lib
+
+
+def _p(a):
+    return a.ctypes.data_as(ctypes.c_void_p) if a is not None else None
+
+
+def neighbor_map(coords, kernel=(3, 3, 3), dilation=1):
+    coords = np.ascontiguousarray(coords, np.int32)
+    n = coords.shape[0]
+    e = lib().orc_neighbor_map(_p(coords), n, *kernel, dilation, None, None, None, 0)
+    src, tgt, kidx = (np.empty(e, np.int64) for _ in range(3))
+    lib().orc_neighbor_map(_p(coords), n, *kernel, dilation, _p(src), _p(tgt), _p(kidx), e)
+    return src, tgt, kidx
+
+
+def csr(n, src, tgt, kidx):
+    e = len(src)
+    rs = np.empty(n + 1, np.int64)
+    ss, ks = np.empty(e, np.int64), np.empty(e, np.int64)
+    lib().orc_csr(n, e, _p(src), _p(tgt), _p(kidx), _p(rs), _p(ss), _p(ks))
+    return rs, ss, ks
+
+
+def conv(x, weight, bias, edges, nthreads=0):
+    """SparseConv3d.forward's CPU loop; weight [Co,Kd,Kh,Kw,Ci]."""
+    x = np.ascontiguousarray(x, np.float32)
+    w = np.ascontiguousarray(weight, np.float32)
+    co, ci = w.shape[0], w.shape[4]
+    ks = w.shape[1] * w.shape[2] * w.shape[3]
+    b = None if bias is None else np.ascontiguousarray(bias, np.float32)
+    src, tgt, kidx = edges
+    out = np.empty((x.shape[0], co), np.float32)
+    lib().orc_conv_forward(_p(x), x.shape[0], ci, _p(w), _p(b), co, ks, _p(src), _p(tgt), _p(kidx), len(src),
+                           _p(out), nthreads)
+    return out
+
+
+def conv_rows(x, weight, bias, csr_arrays, nthreads):
+    x = np.ascontiguousarray(x, np.float32)
+    w = np.ascontiguousarray(weight, np.float32)
+    co, ci = w.shape[0], w.shape[4]
+    ks = w.shape[1] * w.shape[2] * w.shape[3]
+    b = None if bias is None else np.ascontiguousarray(bias, np.float32)
+    rs, ss, kk = csr_arrays
+    out = np.empty((x.shape[0], co), np.float32)
+    lib().orc_conv_forward_rows(_p(x), x.shape[0], ci, _p(w), _p(b), co, ks, _p(rs), _p(ss), _p(kk), _p(out),
+                                nthreads)
+    return out
+
+
+def silu(v):
+    v = np.ascontiguousarray(v, np.float32).copy()
+    lib().orc_silu(_p(v), v.size)
+    return v
+
+
+def round16(v, mode):
+    """mode 'bf16' or 'f16': round to nearest even."""
+    v = np.ascontiguousarray(v, np.float32).copy()
+    lib().orc_round16(_p(v), v.size, 2 if mode == "bf16" else 1)
+    return v
+
+
+def subdivide(coords, sub, positive=False):
+    coords = np.ascontiguousarray(coords, np.int32)
+    sub = np.ascontiguousarray(sub, np.float32)
+    n = coords.shape[0]
+    idx, sidx = np.empty(8 * n, np.int64), np.empty(8 * n, np.int64)
+    nc = np.empty((8 * n, 4), np.int32)
+    m = lib().orc_subdivide(_p(coords), n, _p(sub), int(positive), _p(idx), _p(sidx), _p(nc))
+    return idx[:m].copy(), sidx[:m].copy(), nc[:m].copy()
+
+
+def select_rows(x, idx):
+    x = np.ascontiguousarray(x, np.float32)
+    out = np.empty((len(idx), x.shape[1]), np.float32)
+    lib().orc_select_rows(_p(x), x.shape[1], _p(np.ascontiguousarray(idx, np.int64)), len(idx), _p(out))
+    return out
+
+
+def c2s_unfold(x, idx, subidx):
+    x = np.ascontiguousarray(x, np.float32)
+    cout = x.shape[1] // 8
+    out = np.empty((len(idx), cout), np.float32)
+    lib().orc_c2s_unfold(_p(x), cout, _p(np.ascontiguousarray(idx, np.int64)),
+                         _p(np.ascontiguousarray(subidx, np.int64)), len(idx), _p(out))
+    return out

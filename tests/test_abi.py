@@ -1,0 +1,115 @@
+"""The C-ABI library loads, exports every symbol include/t2sc.h declares,
+and its host-only parts (synthetic inputs, argument checks) behave; no GPU
+compute is called here."""
+import ctypes
+import math
+import os
+import re
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def declared_symbols():
+    src = open(os.path.join(ROOT, "include", "t2sc.h")).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return sorted(set(re.findall(r"\b(t2sc_[a-z0-9_]+)\s*\(", src)))
+
+
+def test_every_declared_symbol_is_exported(t2sc):
+    names = declared_symbols()
+    assert len(names) >= 20
+    raw = ctypes.CDLL(t2sc.LIB_PATH)
+    for n in names:
+        assert hasattr(raw, n), n
+    from t2sc._lib import SIGNATURES
+    assert sorted(SIGNATURES) == names
+
+
+def test_version(t2sc):
+    assert t2sc.lib.t2sc_version().decode().startswith("t2sc")
+
+
+def test_no_gpu_context_fails_cleanly(t2sc):
+    import torch
+    if torch.cuda.is_available():
+        return
+    h = ctypes.c_void_p()
+    rc = t2sc.lib.t2sc_ctx_create(0, ctypes.byref(h))
+    assert rc != 0 and not h.value
+
+
+def _splitmix_xorshift(seed):
+    m = (1 << 64) - 1
+    z = (seed + 0x9E3779B97F4A7C15) & m
+    z = ((z ^ (z >> 30)) * 0xBF58476D1CE4E5B9) & m
+    z = ((z ^ (z >> 27)) * 0x94D049BB133111EB) & m
+    s = z ^ (z >> 31)
+    s = s or 0x9E3779B97F4A7C15
+    while True:
+        x = s
+        x ^= x >> 12
+        x ^= (x << 25) & m
+        x ^= x >> 27
+        s = x
+        yield (x * 0x2545F4914F6CDD1D) & m
+
+
+def test_rng_stream_matches_reference_recipe(t2sc):
+    # trellis2_mojo/rng.mojo:20-44 restated independently in Python
+    g = _splitmix_xorshift(7)
+    ref = []
+    for _ in range(16):
+        u1 = (next(g) >> 11) * 2.0 ** -53
+        while u1 == 0.0:
+            u1 = (next(g) >> 11) * 2.0 ** -53
+        u2 = (next(g) >> 11) * 2.0 ** -53
+        ref.append(math.sqrt(-2.0 * math.log(u1)) * math.cos(6.283185307179586 * u2))
+    got = t2sc.synth.normal(7, (16,))
+    assert np.allclose(got, np.array(ref, np.float32), rtol=1e-6, atol=1e-7)
+    g = _splitmix_xorshift(9)
+    ref_b = [1.0 if (next(g) >> 11) * 2.0 ** -53 < 0.5 else 0.0 for _ in range(64)]
+    assert t2sc.synth.bernoulli(9, (64,)).tolist() == ref_b
+
+
+def test_shell_sizes_and_order(t2sc):
+    # sizes of the benchmark shells with this generator (cfg4 matches the
+    # 503,562 calibrated for the 512^3 configuration)
+    expect = {"cfg1": 14454, "cfg2": 101422, "cfg3_parent": 51982, "cfg4": 503562}
+    for k, n in expect.items():
+        c = t2sc.synth.shell(*t2sc.synth.SHELLS[k])
+        assert len(c) == n, k
+        if k == "cfg1":
+            key = ((c[:, 1].astype(np.int64) * 4096) + c[:, 2]) * 4096 + c[:, 3]
+            assert np.all(np.diff(key) > 0)  # lexicographic, unique
+            assert np.all(c[:, 0] == 0)
+
+
+def test_shell_seed_changes_phase(t2sc):
+    a = t2sc.synth.shell(64, 24.0, 1.0, seed=0)
+    b = t2sc.synth.shell(64, 24.0, 1.0, seed=1)
+    assert not (len(a) == len(b) and np.array_equal(a, b))
+
+
+def test_lcg_fill_matches_reference_test_helper(t2sc):
+    # parity_wp11_gpu_conv.mojo:22-27, first values computed by the scalar recurrence
+    m = (1 << 64) - 1
+    a, c = 6364136223846793005, 1442695040888963407
+    s = (41 * a + c) & m
+    ref = []
+    for _ in range(5000):
+        s = (s * a + c) & m
+        u = np.float32((s >> 33) & ((1 << 20) - 1)) / np.float32(1 << 19)
+        ref.append((u - np.float32(1.0)) * np.float32(0.05))
+    assert np.array_equal(t2sc.synth.lcg_fill((5000,), 41, 0.05), np.array(ref, np.float32))
+
+
+def test_host_mirror_argument_errors(t2sc):
+    import pytest
+    with pytest.raises(ValueError):
+        t2sc.SparseTensor(np.zeros((2, 4)), np.array([[1, 0, 0, 0], [0, 0, 0, 1]]))  # batches out of order
+    with pytest.raises(ValueError):
+        t2sc.SparseTensor(np.zeros((3, 4)), np.zeros((2, 4)))
+    with pytest.raises(ValueError):
+        t2sc.SparseConv3d(np.zeros((4, 3, 3, 4)), np.zeros(4))  # weight must be 5-D

@@ -1,0 +1,142 @@
+"""The CPU restatement (oracle) against everything that pins it: the
+reference's published dense-blob edge counts, hand-computed known answers
+for the map / CSR / subdivision order, and the committed golden fixtures."""
+import numpy as np
+import pytest
+
+
+def blob(side):
+    z, y, x = np.meshgrid(np.arange(side), np.arange(side), np.arange(side), indexing="ij")
+    out = np.zeros((side ** 3, 4), np.int32)
+    out[:, 1], out[:, 2], out[:, 3] = x.ravel() + 4, y.ravel() + 4, z.ravel() + 4
+    return out
+
+
+# docs/benchmarks/RESULTS.md:363-365 of the reference: N -> E for dense blobs
+@pytest.mark.parametrize("side,n,e", [(23, 12167, 300763), (38, 54872, 1404928), (60, 216000, 5639752)])
+def test_published_edge_counts(oracle, side, n, e):
+    c = blob(side)
+    assert len(c) == n
+    src, tgt, kidx = oracle.neighbor_map(c)
+    assert len(src) == e == (3 * side - 2) ** 3
+
+
+def test_pack_key(oracle):
+    L = oracle.lib()
+    assert L.orc_pack_key(0, 0, 0, 0) == ((512 * 2048) + 512) * 2048 + 512
+    assert L.orc_pack_key(1, 2, 3, 4) == ((1 * 2048 + 2 + 512) * 2048 + 3 + 512) * 2048 + 4 + 512
+
+
+def test_map_order_known_answer(oracle):
+    # two voxels adjacent along column 3 (+z in the kx slot)
+    c = np.array([[0, 5, 5, 5], [0, 5, 5, 6]], np.int32)
+    src, tgt, kidx = oracle.neighbor_map(c)
+    # k = kz*9+ky*3+kx, offsets (kz-1, ky-1, kx-1) on columns 1,2,3
+    # row1 sees row0 at offset col3 -1 -> k = 9+3+0 = 12; self at k = 13;
+    # row0 sees row1 at offset col3 +1 -> k = 14
+    assert list(kidx) == [12, 13, 13, 14]
+    assert list(tgt) == [1, 0, 1, 0]
+    assert list(src) == [0, 0, 1, 1]
+    rs, ss, ks = oracle.csr(2, src, tgt, kidx)
+    assert list(rs) == [0, 2, 4]
+    assert list(ks) == [13, 14, 12, 13]
+    assert list(ss) == [0, 1, 0, 1]
+
+
+def test_duplicates_last_row_wins(oracle):
+    c = np.array([[0, 1, 1, 1], [0, 1, 1, 1]], np.int32)
+    src, tgt, kidx = oracle.neighbor_map(c)
+    assert list(src) == [1, 1] and list(tgt) == [0, 1] and list(kidx) == [13, 13]
+
+
+def test_batches_do_not_mix(oracle):
+    c = np.array([[0, 1, 1, 1], [1, 1, 1, 2]], np.int32)
+    src, tgt, kidx = oracle.neighbor_map(c)
+    assert list(kidx) == [13, 13]
+
+
+def test_dilation(oracle):
+    c = np.array([[0, 0, 0, 0], [0, 2, 0, 0], [0, 1, 0, 0]], np.int32)
+    src, tgt, kidx = oracle.neighbor_map(c, dilation=2)
+    pairs = sorted(zip(src.tolist(), tgt.tolist(), kidx.tolist()))
+    # rows 0 and 1 are two apart along column 1 -> offsets kz = 0/2 (k = 4 / 22)
+    assert (0, 1, 4) in pairs and (1, 0, 22) in pairs and (2, 2, 13) in pairs
+    assert len(pairs) == 5
+
+
+def test_conv_matches_float64(oracle):
+    rng = np.random.default_rng(0)
+    c = blob(5)
+    n, ci, co = len(c), 24, 40
+    x = rng.standard_normal((n, ci)).astype(np.float32)
+    w = (rng.standard_normal((co, 3, 3, 3, ci)) * 0.1).astype(np.float32)
+    b = rng.standard_normal(co).astype(np.float32)
+    e = oracle.neighbor_map(c)
+    y = oracle.conv(x, w, b, e)
+    src, tgt, kidx = e
+    ref = np.zeros((n, co))
+    wk = w.reshape(co, 27, ci).astype(np.float64)
+    for s, t, k in zip(src, tgt, kidx):
+        ref[t] += wk[:, k, :] @ x[s].astype(np.float64)
+    ref += b
+    assert np.max(np.abs(y - ref)) / np.max(np.abs(ref)) < 1e-6
+
+
+def test_conv_row_parallel_is_bit_identical(oracle):
+    rng = np.random.default_rng(1)
+    c = blob(6)
+    x = rng.standard_normal((len(c), 20)).astype(np.float32)
+    w = rng.standard_normal((16, 3, 3, 3, 20)).astype(np.float32)
+    b = rng.standard_normal(16).astype(np.float32)
+    e = oracle.neighbor_map(c)
+    y1 = oracle.conv(x, w, b, e, nthreads=1)
+    y2 = oracle.conv(x, w, b, e, nthreads=0)
+    y3 = oracle.conv_rows(x, w, b, oracle.csr(len(c), *e), nthreads=4)
+    assert np.array_equal(y1, y2) and np.array_equal(y1, y3)
+
+
+def test_subdivision_known_answer(oracle):
+    c = np.array([[0, 1, 2, 3], [0, 4, 4, 4]], np.int32)
+    sub = np.zeros((2, 8), np.float32)
+    sub[0, [0, 5, 7]] = 1.0
+    sub[1, 3] = -0.5  # nonzero -> kept by forward_subdivision, dropped by binarize
+    idx, sidx, nc = oracle.subdivide(c, sub)
+    assert list(idx) == [0, 0, 0, 1] and list(sidx) == [0, 5, 7, 3]
+    assert nc.tolist() == [[0, 2, 4, 6], [0, 3, 4, 7], [0, 3, 5, 7], [0, 9, 9, 8]]
+    idx, sidx, nc = oracle.subdivide(c, sub, positive=True)
+    assert list(idx) == [0, 0, 0]
+    x = np.arange(2 * 16, dtype=np.float32).reshape(2, 16)
+    out = oracle.c2s_unfold(x, [0, 1], [5, 3])
+    assert out.tolist() == [x[0, 10:12].tolist(), x[1, 6:8].tolist()]
+    assert oracle.select_rows(x, [1, 0]).tolist() == [x[1].tolist(), x[0].tolist()]
+
+
+def test_silu_formula(oracle):
+    v = np.linspace(-20, 20, 101).astype(np.float32)
+    ref = v.astype(np.float64) / (1 + np.exp(-v.astype(np.float64)))
+    assert np.allclose(oracle.silu(v), ref, rtol=1e-6, atol=1e-7)
+
+
+def test_round16(oracle):
+    import torch
+    v = np.random.default_rng(2).standard_normal(10000).astype(np.float32) * 100
+    v[:4] = [65519.0, 65520.0, 1e-8, -3e-5]
+    for mode, dt in (("bf16", torch.bfloat16), ("f16", torch.float16)):
+        ref = torch.from_numpy(v).to(dt).float().numpy()
+        assert np.array_equal(oracle.round16(v, mode), ref), mode
+
+
+def test_golden_fixtures(oracle):
+    import os
+    d = os.path.join(os.path.dirname(__file__), "golden")
+    g = np.load(os.path.join(d, "small_cases.npz"))
+    for case in ("shell16", "blob4d2"):
+        c = g[case + "_coords"]
+        dil = int(g[case + "_dil"])
+        src, tgt, kidx = oracle.neighbor_map(c, dilation=dil)
+        assert np.array_equal(src, g[case + "_src"]) and np.array_equal(tgt, g[case + "_tgt"])
+        assert np.array_equal(kidx, g[case + "_kidx"])
+        y = oracle.conv(g[case + "_x"], g[case + "_w"], g[case + "_b"], (src, tgt, kidx))
+        assert np.array_equal(y, g[case + "_y"])
+    idx, sidx, nc = oracle.subdivide(g["sub_coords"], g["sub_mask"])
+    assert np.array_equal(nc, g["sub_out_coords"]) and np.array_equal(idx, g["sub_idx"])

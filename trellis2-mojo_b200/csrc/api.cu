@@ -1,0 +1,496 @@
+// C-ABI entry points of libt2sc (declared in include/t2sc.h).
+#include <stdio.h>
+
+#include <new>
+#include <vector>
+
+#include "internal.h"
+
+using namespace t2sc;
+
+namespace {
+
+// Makes the context's device current for the duration of a call and
+// restores the caller's device afterwards.
+struct DeviceGuard {
+  int prev = -1;
+  explicit DeviceGuard(int dev) {
+    if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+    if (prev != dev) cudaSetDevice(dev);
+  }
+  ~DeviceGuard() {
+    int cur = -1;
+    if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+  }
+};
+
+int fail(t2sc_ctx *ctx, int code, const std::string &msg) {
+  if (ctx) ctx->last_error = msg;
+  return code;
+}
+
+size_t elem_size(int dtype) { return dtype == T2SC_DT_F32 ? 4 : 2; }
+
+// Stream-ordered temporary device buffer.
+struct DevBuf {
+  void *p = nullptr;
+  cudaStream_t st = nullptr;
+  DevBuf() = default;
+  DevBuf(const DevBuf &) = delete;
+  ~DevBuf() {
+    if (p) cudaFreeAsync(p, st);
+  }
+  int alloc(t2sc_ctx *ctx, size_t bytes) {
+    st = ctx->stream;
+    std::string &err = ctx->last_error;
+    T2SC_CUDA(cudaMallocAsync(&p, bytes ? bytes : 16, st), "device buffer");
+    return T2SC_OK;
+  }
+};
+
+#define T2SC_TRY(expr)                   \
+  do {                                   \
+    int _rc = (expr);                    \
+    if (_rc != T2SC_OK) return _rc;      \
+  } while (0)
+
+// Runs an entry point's body; C++ exceptions never cross the C ABI.
+template <class F>
+int guarded(t2sc_ctx *ctx, F &&body) {
+  try {
+    return body();
+  } catch (const std::bad_alloc &) {
+    return fail(ctx, T2SC_ERR_OOM, "host allocation failed");
+  } catch (...) {
+    return fail(ctx, T2SC_ERR_INVALID, "unexpected exception");
+  }
+}
+
+int check_sync(t2sc_ctx *ctx) {
+  std::string &err = ctx->last_error;
+  T2SC_CUDA(cudaStreamSynchronize(ctx->stream), "stream synchronize");
+  int flags = 0;
+  T2SC_TRY(read_dev_err(ctx, &flags));
+  if (flags & kDevErrTimeout)
+    return fail(ctx, T2SC_ERR_TIMEOUT, "a bounded device wait timed out; results of the last call are invalid");
+  if (flags) return fail(ctx, T2SC_ERR_INVALID, "device error flags set: " + std::to_string(flags));
+  return T2SC_OK;
+}
+
+}  // namespace
+
+int t2sc::read_dev_err(t2sc_ctx *ctx, int *flags) {
+  std::string &err = ctx->last_error;
+  int h = 0;
+  T2SC_CUDA(cudaMemcpyAsync(&h, ctx->d_err, sizeof(int), cudaMemcpyDeviceToHost, ctx->stream), "read error flags");
+  T2SC_CUDA(cudaStreamSynchronize(ctx->stream), "read error flags");
+  if (h) T2SC_CUDA(cudaMemsetAsync(ctx->d_err, 0, sizeof(int), ctx->stream), "clear error flags");
+  *flags = h;
+  return T2SC_OK;
+}
+
+extern "C" {
+
+const char *t2sc_version(void) { return "t2sc 0.1 sm_100a"; }
+
+int t2sc_ctx_create(int device, t2sc_ctx **out) {
+  if (!out) return T2SC_ERR_INVALID;
+  *out = nullptr;
+  return guarded(nullptr, [&]() -> int {
+    int ndev = 0;
+    if (cudaGetDeviceCount(&ndev) != cudaSuccess || device < 0 || device >= ndev) return T2SC_ERR_CUDA;
+    DeviceGuard g(device);
+    cudaDeviceProp prop;
+    if (cudaGetDeviceProperties(&prop, device) != cudaSuccess) return T2SC_ERR_CUDA;
+    if (prop.major != 10) return T2SC_ERR_UNSUPPORTED;  // built for sm_100a only
+    std::unique_ptr<t2sc_ctx> ctx(new t2sc_ctx());
+    ctx->device = device;
+    ctx->num_sms = prop.multiProcessorCount;
+    if (cudaStreamCreateWithFlags(&ctx->own_stream, cudaStreamNonBlocking) != cudaSuccess) return T2SC_ERR_CUDA;
+    ctx->stream = ctx->own_stream;
+    if (cudaMalloc((void **)&ctx->d_err, sizeof(int)) != cudaSuccess) return T2SC_ERR_OOM;
+    if (cudaMemset(ctx->d_err, 0, sizeof(int)) != cudaSuccess) return T2SC_ERR_CUDA;
+    *out = ctx.release();
+    return T2SC_OK;
+  });
+}
+
+int t2sc_ctx_destroy(t2sc_ctx *ctx) {
+  if (!ctx) return T2SC_OK;
+  DeviceGuard g(ctx->device);
+  cudaStreamSynchronize(ctx->stream);
+  cudaFree(ctx->d_err);
+  if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
+  delete ctx;
+  return T2SC_OK;
+}
+
+int t2sc_ctx_set_stream(t2sc_ctx *ctx, void *stream) {
+  if (!ctx) return T2SC_ERR_INVALID;
+  ctx->stream = stream ? static_cast<cudaStream_t>(stream) : ctx->own_stream;
+  return T2SC_OK;
+}
+
+int t2sc_ctx_synchronize(t2sc_ctx *ctx) {
+  if (!ctx) return T2SC_ERR_INVALID;
+  DeviceGuard g(ctx->device);
+  return check_sync(ctx);
+}
+
+const char *t2sc_last_error(const t2sc_ctx *ctx) { return ctx ? ctx->last_error.c_str() : "null context"; }
+
+int t2sc_ctx_launch_count(const t2sc_ctx *ctx, int64_t *count) {
+  if (!ctx || !count) return T2SC_ERR_INVALID;
+  *count = ctx->launches;
+  return T2SC_OK;
+}
+
+// ------------------------------- coordinates -------------------------------
+
+static int coords_create_impl(t2sc_ctx *ctx, const int32_t *coords, int64_t n, bool on_device,
+                              t2sc_coords **out) {
+  if (!ctx || !out) return T2SC_ERR_INVALID;
+  *out = nullptr;
+  if (n < 0 || (n > 0 && !coords)) return fail(ctx, T2SC_ERR_INVALID, "coords: bad pointer or count");
+  if (n >= (int64_t(1) << 31)) return fail(ctx, T2SC_ERR_UNSUPPORTED, "coords: more than 2^31-1 rows");
+  return guarded(ctx, [&]() -> int {
+    DeviceGuard g(ctx->device);
+    std::string &err = ctx->last_error;
+    std::unique_ptr<t2sc_coords> c(new t2sc_coords());
+    c->ctx = ctx;
+    c->n = n;
+    T2SC_CUDA(cudaMalloc((void **)&c->d_coords, (size_t)(n > 0 ? n : 1) * 16), "coords");
+    if (n > 0)
+      T2SC_CUDA(cudaMemcpyAsync(c->d_coords, coords, (size_t)n * 16,
+                                on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, ctx->stream),
+                "coords upload");
+    int rc = build_hash(c.get(), err);
+    if (rc != T2SC_OK) {
+      t2sc_coords_destroy(c.release());
+      return rc;
+    }
+    *out = c.release();
+    return T2SC_OK;
+  });
+}
+
+int t2sc_coords_create(t2sc_ctx *ctx, const int32_t *coords, int64_t n, t2sc_coords **out) {
+  return coords_create_impl(ctx, coords, n, false, out);
+}
+int t2sc_coords_create_device(t2sc_ctx *ctx, const int32_t *coords, int64_t n, t2sc_coords **out) {
+  return coords_create_impl(ctx, coords, n, true, out);
+}
+
+int t2sc_coords_destroy(t2sc_coords *c) {
+  if (!c) return T2SC_OK;
+  DeviceGuard g(c->ctx->device);
+  cudaStreamSynchronize(c->ctx->stream);
+  for (auto &kv : c->maps) free_map(kv.second);
+  cudaFree(c->d_coords);
+  cudaFree(c->d_keys);
+  cudaFree(c->d_vals);
+  delete c;
+  return T2SC_OK;
+}
+
+int t2sc_coords_count(const t2sc_coords *c, int64_t *n) {
+  if (!c || !n) return T2SC_ERR_INVALID;
+  *n = c->n;
+  return T2SC_OK;
+}
+
+static int kernel_ok(t2sc_ctx *ctx, int kd, int kh, int kw, int dil) {
+  if (kd < 1 || kh < 1 || kw < 1 || kd * kh * kw > kMaxK)
+    return fail(ctx, T2SC_ERR_UNSUPPORTED, "kernel volume must be 1..32");
+  if (dil < 1 || dil > 512) return fail(ctx, T2SC_ERR_INVALID, "dilation must be >= 1");
+  return T2SC_OK;
+}
+
+int t2sc_coords_build_map(t2sc_coords *c, int kd, int kh, int kw, int dil, int64_t *n_edges) {
+  if (!c) return T2SC_ERR_INVALID;
+  t2sc_ctx *ctx = c->ctx;
+  T2SC_TRY(kernel_ok(ctx, kd, kh, kw, dil));
+  return guarded(ctx, [&]() -> int {
+    DeviceGuard g(ctx->device);
+    t2sc_map *m = nullptr;
+    T2SC_TRY(build_map(c, kd, kh, kw, dil, &m, ctx->last_error));
+    if (n_edges) *n_edges = m->n_edges;
+    return T2SC_OK;
+  });
+}
+
+int t2sc_neighbor_map_export(t2sc_coords *c, int kd, int kh, int kw, int dil, int64_t *src, int64_t *tgt,
+                             int64_t *kidx, int64_t cap, int64_t *n_edges) {
+  if (!c || !n_edges) return T2SC_ERR_INVALID;
+  t2sc_ctx *ctx = c->ctx;
+  T2SC_TRY(kernel_ok(ctx, kd, kh, kw, dil));
+  return guarded(ctx, [&]() -> int {
+    DeviceGuard g(ctx->device);
+    t2sc_map *m = nullptr;
+    T2SC_TRY(build_map(c, kd, kh, kw, dil, &m, ctx->last_error));
+    *n_edges = m->n_edges;
+    if (m->n_edges > cap) return fail(ctx, T2SC_ERR_CAPACITY, "edge buffers too small");
+    if (m->n_edges > 0 && (!src || !tgt || !kidx)) return fail(ctx, T2SC_ERR_INVALID, "null edge buffer");
+    T2SC_TRY(export_edges(c, m, src, tgt, kidx, ctx->last_error));
+    return check_sync(ctx);
+  });
+}
+
+int t2sc_csr_export(t2sc_coords *c, int kd, int kh, int kw, int dil, int64_t *row_start, int64_t *src_s,
+                    int64_t *kidx_s, int64_t cap, int64_t *n_edges) {
+  if (!c || !n_edges || !row_start) return T2SC_ERR_INVALID;
+  t2sc_ctx *ctx = c->ctx;
+  T2SC_TRY(kernel_ok(ctx, kd, kh, kw, dil));
+  return guarded(ctx, [&]() -> int {
+    DeviceGuard g(ctx->device);
+    t2sc_map *m = nullptr;
+    T2SC_TRY(build_map(c, kd, kh, kw, dil, &m, ctx->last_error));
+    *n_edges = m->n_edges;
+    if (m->n_edges > cap) return fail(ctx, T2SC_ERR_CAPACITY, "edge buffers too small");
+    if (m->n_edges > 0 && (!src_s || !kidx_s)) return fail(ctx, T2SC_ERR_INVALID, "null edge buffer");
+    T2SC_TRY(export_csr(c, m, row_start, src_s, kidx_s, ctx->last_error));
+    return check_sync(ctx);
+  });
+}
+
+// ---------------------------------- conv ----------------------------------
+
+int t2sc_conv_create(t2sc_ctx *ctx, const float *weight, const float *bias, int co, int kd, int kh, int kw, int ci,
+                     int dilation, int dtype, t2sc_conv **out) {
+  if (!ctx || !out) return T2SC_ERR_INVALID;
+  *out = nullptr;
+  T2SC_TRY(kernel_ok(ctx, kd, kh, kw, dilation));
+  if (!weight || co <= 0 || ci <= 0) return fail(ctx, T2SC_ERR_INVALID, "conv: need weight and positive Co, Ci");
+  if (dtype != T2SC_DT_F32 && dtype != T2SC_DT_F16 && dtype != T2SC_DT_BF16)
+    return fail(ctx, T2SC_ERR_INVALID, "conv: unknown dtype");
+  return guarded(ctx, [&]() -> int {
+    DeviceGuard g(ctx->device);
+    std::string &err = ctx->last_error;
+    std::unique_ptr<t2sc_conv> cv(new t2sc_conv());
+    cv->ctx = ctx;
+    cv->co = co;
+    cv->ci = ci;
+    cv->kd = kd;
+    cv->kh = kh;
+    cv->kw = kw;
+    cv->kvol = kd * kh * kw;
+    cv->dilation = dilation;
+    cv->dtype = dtype;
+    cv->has_bias = bias != nullptr;
+    std::vector<float> b(co, 0.0f);
+    if (bias)
+      for (int o = 0; o < co; o++) b[o] = bias[o];
+    int rc;
+    if ((rc = t2sc::cuda_status(cudaMalloc((void **)&cv->d_bias, co * sizeof(float)), err, "bias")) != T2SC_OK ||
+        (rc = t2sc::cuda_status(cudaMemcpy(cv->d_bias, b.data(), co * sizeof(float), cudaMemcpyHostToDevice), err,
+                                "bias upload")) != T2SC_OK) {
+      t2sc_conv_destroy(cv.release());
+      return rc;
+    }
+    cv->tc_path = (dtype != T2SC_DT_F32 && ci % 8 == 0 && co % 16 == 0) ? 1 : 0;
+    rc = cv->tc_path ? conv_tc_prepare(cv.get(), weight, err) : conv_simt_prepare(cv.get(), weight, err);
+    if (rc != T2SC_OK) {
+      t2sc_conv_destroy(cv.release());
+      return rc;
+    }
+    *out = cv.release();
+    return T2SC_OK;
+  });
+}
+
+int t2sc_conv_destroy(t2sc_conv *cv) {
+  if (!cv) return T2SC_OK;
+  DeviceGuard g(cv->ctx->device);
+  cudaStreamSynchronize(cv->ctx->stream);
+  cudaFree(cv->d_bias);
+  cudaFree(cv->d_wtc);
+  cudaFree(cv->d_w_simt);
+  cudaFree(cv->d_w_lo);
+  delete cv;
+  return T2SC_OK;
+}
+
+static int forward_device_impl(t2sc_conv *cv, t2sc_coords *c, const void *x, void *y, int flags,
+                               const void *residual) {
+  t2sc_ctx *ctx = cv->ctx;
+  if (c->ctx != ctx) return fail(ctx, T2SC_ERR_INVALID, "conv and coords belong to different contexts");
+  if (flags & ~(T2SC_SILU | T2SC_RESIDUAL)) return fail(ctx, T2SC_ERR_INVALID, "unknown flags");
+  if ((flags & T2SC_RESIDUAL) && !residual) return fail(ctx, T2SC_ERR_INVALID, "RESIDUAL flag without residual");
+  if (c->n > 0 && (!x || !y)) return fail(ctx, T2SC_ERR_INVALID, "null feature buffer");
+  t2sc_map *m = nullptr;
+  T2SC_TRY(build_map(c, cv->kd, cv->kh, cv->kw, cv->dilation, &m, ctx->last_error));
+  return cv->tc_path ? conv_tc_launch(cv, m, x, y, flags, residual, ctx->last_error)
+                     : conv_simt_launch(cv, m, x, y, flags, residual, ctx->last_error);
+}
+
+int t2sc_conv_forward_device(t2sc_conv *cv, t2sc_coords *c, const void *x, void *y, int flags,
+                             const void *residual) {
+  if (!cv || !c) return T2SC_ERR_INVALID;
+  return guarded(cv->ctx, [&]() -> int {
+    DeviceGuard g(cv->ctx->device);
+    return forward_device_impl(cv, c, x, y, flags, residual);
+  });
+}
+
+// Host f32 [count] -> device buffer of `dtype` (staging through `tmp32`).
+static int upload_as(t2sc_ctx *ctx, const float *h, int64_t count, int dtype, DevBuf &dst) {
+  std::string &err = ctx->last_error;
+  T2SC_TRY(dst.alloc(ctx, count * elem_size(dtype)));
+  if (dtype == T2SC_DT_F32) {
+    T2SC_CUDA(cudaMemcpyAsync(dst.p, h, count * 4, cudaMemcpyHostToDevice, ctx->stream), "upload");
+    return T2SC_OK;
+  }
+  DevBuf tmp;
+  T2SC_TRY(tmp.alloc(ctx, count * 4));
+  T2SC_CUDA(cudaMemcpyAsync(tmp.p, h, count * 4, cudaMemcpyHostToDevice, ctx->stream), "upload");
+  return f32_to_dtype(ctx, (const float *)tmp.p, dst.p, count, dtype);
+}
+
+static int download_as(t2sc_ctx *ctx, const void *d, int64_t count, int dtype, float *h) {
+  std::string &err = ctx->last_error;
+  if (dtype == T2SC_DT_F32) {
+    T2SC_CUDA(cudaMemcpyAsync(h, d, count * 4, cudaMemcpyDeviceToHost, ctx->stream), "download");
+    return T2SC_OK;
+  }
+  DevBuf tmp;
+  T2SC_TRY(tmp.alloc(ctx, count * 4));
+  T2SC_TRY(dtype_to_f32(ctx, d, (float *)tmp.p, count, dtype));
+  T2SC_CUDA(cudaMemcpyAsync(h, tmp.p, count * 4, cudaMemcpyDeviceToHost, ctx->stream), "download");
+  return T2SC_OK;
+}
+
+int t2sc_conv_forward(t2sc_conv *cv, t2sc_coords *c, const float *x, float *y, int flags, const float *residual) {
+  if (!cv || !c) return T2SC_ERR_INVALID;
+  t2sc_ctx *ctx = cv->ctx;
+  return guarded(ctx, [&]() -> int {
+    DeviceGuard g(ctx->device);
+    const int64_t n = c->n;
+    if (n == 0) return T2SC_OK;
+    if (!x || !y) return fail(ctx, T2SC_ERR_INVALID, "null feature buffer");
+    if ((flags & T2SC_RESIDUAL) && !residual) return fail(ctx, T2SC_ERR_INVALID, "RESIDUAL flag without residual");
+    DevBuf dx, dy, dr;
+    T2SC_TRY(upload_as(ctx, x, n * cv->ci, cv->dtype, dx));
+    if (flags & T2SC_RESIDUAL) T2SC_TRY(upload_as(ctx, residual, n * cv->co, cv->dtype, dr));
+    T2SC_TRY(dy.alloc(ctx, n * cv->co * elem_size(cv->dtype)));
+    T2SC_TRY(forward_device_impl(cv, c, dx.p, dy.p, flags, dr.p));
+    T2SC_TRY(download_as(ctx, dy.p, n * cv->co, cv->dtype, y));
+    return check_sync(ctx);
+  });
+}
+
+int t2sc_conv_chain_forward(t2sc_conv *const *convs, int n_layers, t2sc_coords *c, const float *x, float *y,
+                            const int *flags) {
+  if (!convs || n_layers <= 0 || !c || !convs[0]) return T2SC_ERR_INVALID;
+  t2sc_ctx *ctx = convs[0]->ctx;
+  return guarded(ctx, [&]() -> int {
+    DeviceGuard g(ctx->device);
+    const int dtype = convs[0]->dtype;
+    int cmax = convs[0]->ci;
+    for (int i = 0; i < n_layers; i++) {
+      if (!convs[i] || convs[i]->ctx != ctx || convs[i]->dtype != dtype)
+        return fail(ctx, T2SC_ERR_INVALID, "chain: convs must share context and dtype");
+      if (i > 0 && convs[i]->ci != convs[i - 1]->co)
+        return fail(ctx, T2SC_ERR_INVALID, "chain: Ci of a layer must equal Co of the previous one");
+      int f = flags ? flags[i] : 0;
+      if ((f & T2SC_RESIDUAL) && convs[i]->co != convs[0]->ci)
+        return fail(ctx, T2SC_ERR_INVALID, "chain: residual layer needs Co equal to the chain input width");
+      cmax = convs[i]->co > cmax ? convs[i]->co : cmax;
+    }
+    const int64_t n = c->n;
+    if (n == 0) return T2SC_OK;
+    if (!x || !y) return fail(ctx, T2SC_ERR_INVALID, "null feature buffer");
+    DevBuf din, b0, b1;
+    T2SC_TRY(upload_as(ctx, x, n * convs[0]->ci, dtype, din));
+    T2SC_TRY(b0.alloc(ctx, n * cmax * elem_size(dtype)));
+    T2SC_TRY(b1.alloc(ctx, n * cmax * elem_size(dtype)));
+    const void *cur = din.p;
+    void *bufs[2] = {b0.p, b1.p};
+    for (int i = 0; i < n_layers; i++) {
+      int f = flags ? flags[i] : 0;
+      void *out = bufs[i & 1];
+      T2SC_TRY(forward_device_impl(convs[i], c, cur, out, f, (f & T2SC_RESIDUAL) ? din.p : nullptr));
+      cur = out;
+    }
+    T2SC_TRY(download_as(ctx, cur, n * convs[n_layers - 1]->co, dtype, y));
+    return check_sync(ctx);
+  });
+}
+
+// ------------------------------- subdivision -------------------------------
+
+static int sub_args_ok(t2sc_ctx *ctx, int64_t n, const int32_t *coords, const float *sub, int keep_mode,
+                       const void *feats, int c, int feats_mode, const int32_t *out_coords, const void *out_feats,
+                       const int64_t *m) {
+  if (!m) return fail(ctx, T2SC_ERR_INVALID, "subdivide: null m");
+  if (n < 0 || (n > 0 && (!coords || !sub || !out_coords))) return fail(ctx, T2SC_ERR_INVALID, "subdivide: null input");
+  if (n >= (int64_t(1) << 28)) return fail(ctx, T2SC_ERR_UNSUPPORTED, "subdivide: more than 2^28 parents");
+  if (keep_mode != T2SC_SUB_NONZERO && keep_mode != T2SC_SUB_POSITIVE)
+    return fail(ctx, T2SC_ERR_INVALID, "subdivide: unknown keep mode");
+  if (feats_mode != T2SC_FEATS_NONE && feats_mode != T2SC_FEATS_UPSAMPLE && feats_mode != T2SC_FEATS_C2S)
+    return fail(ctx, T2SC_ERR_INVALID, "subdivide: unknown feature mode");
+  if (feats_mode != T2SC_FEATS_NONE && n > 0 && (!feats || !out_feats || c <= 0))
+    return fail(ctx, T2SC_ERR_INVALID, "subdivide: feature buffers and C > 0 required");
+  return T2SC_OK;
+}
+
+int t2sc_subdivide_device(t2sc_ctx *ctx, const int32_t *coords, int64_t n, const float *sub, int keep_mode,
+                          const void *feats, int c, int feats_mode, int dtype, int32_t *out_coords, void *out_feats,
+                          int32_t *out_parent, int32_t *out_subidx, int64_t *m) {
+  if (!ctx) return T2SC_ERR_INVALID;
+  T2SC_TRY(sub_args_ok(ctx, n, coords, sub, keep_mode, feats, c, feats_mode, out_coords, out_feats, m));
+  if (dtype != T2SC_DT_F32 && dtype != T2SC_DT_F16 && dtype != T2SC_DT_BF16)
+    return fail(ctx, T2SC_ERR_INVALID, "subdivide: unknown dtype");
+  return guarded(ctx, [&]() -> int {
+    DeviceGuard g(ctx->device);
+    return subdivide_device(ctx, coords, n, sub, keep_mode, feats, c, feats_mode, dtype, out_coords, out_feats,
+                            out_parent, out_subidx, m, ctx->last_error);
+  });
+}
+
+int t2sc_subdivide(t2sc_ctx *ctx, const int32_t *coords, int64_t n, const float *sub, int keep_mode,
+                   const float *feats, int c, int feats_mode, int32_t *out_coords, float *out_feats,
+                   int64_t *out_parent, int64_t *out_subidx, int64_t *m) {
+  if (!ctx) return T2SC_ERR_INVALID;
+  T2SC_TRY(sub_args_ok(ctx, n, coords, sub, keep_mode, feats, c, feats_mode, out_coords, out_feats, m));
+  return guarded(ctx, [&]() -> int {
+    DeviceGuard g(ctx->device);
+    std::string &err = ctx->last_error;
+    *m = 0;
+    if (n == 0) return T2SC_OK;
+    const int64_t fin = feats_mode == T2SC_FEATS_C2S ? 8 * (int64_t)c : c;
+    DevBuf dc, ds, dfi, dco, dfo, dpar, dsub;
+    T2SC_TRY(dc.alloc(ctx, n * 16));
+    T2SC_TRY(ds.alloc(ctx, n * 32));
+    T2SC_TRY(dco.alloc(ctx, 8 * n * 16));
+    T2SC_TRY(dpar.alloc(ctx, 8 * n * 4));
+    T2SC_TRY(dsub.alloc(ctx, 8 * n * 4));
+    T2SC_CUDA(cudaMemcpyAsync(dc.p, coords, n * 16, cudaMemcpyHostToDevice, ctx->stream), "subdivide upload");
+    T2SC_CUDA(cudaMemcpyAsync(ds.p, sub, n * 32, cudaMemcpyHostToDevice, ctx->stream), "subdivide upload");
+    if (feats_mode != T2SC_FEATS_NONE) {
+      T2SC_TRY(dfi.alloc(ctx, n * fin * 4));
+      T2SC_TRY(dfo.alloc(ctx, 8 * n * (int64_t)c * 4));
+      T2SC_CUDA(cudaMemcpyAsync(dfi.p, feats, n * fin * 4, cudaMemcpyHostToDevice, ctx->stream), "subdivide upload");
+    }
+    int64_t mm = 0;
+    T2SC_TRY(subdivide_device(ctx, (const int32_t *)dc.p, n, (const float *)ds.p, keep_mode, dfi.p, c, feats_mode,
+                              T2SC_DT_F32, (int32_t *)dco.p, dfo.p, (int32_t *)dpar.p, (int32_t *)dsub.p, &mm, err));
+    std::vector<int32_t> par(out_parent ? mm : 0), sid(out_subidx ? mm : 0);
+    if (mm > 0) {
+      T2SC_CUDA(cudaMemcpyAsync(out_coords, dco.p, mm * 16, cudaMemcpyDeviceToHost, ctx->stream), "subdivide dl");
+      if (feats_mode != T2SC_FEATS_NONE)
+        T2SC_CUDA(cudaMemcpyAsync(out_feats, dfo.p, mm * (int64_t)c * 4, cudaMemcpyDeviceToHost, ctx->stream),
+                  "subdivide dl");
+      if (out_parent)
+        T2SC_CUDA(cudaMemcpyAsync(par.data(), dpar.p, mm * 4, cudaMemcpyDeviceToHost, ctx->stream), "subdivide dl");
+      if (out_subidx)
+        T2SC_CUDA(cudaMemcpyAsync(sid.data(), dsub.p, mm * 4, cudaMemcpyDeviceToHost, ctx->stream), "subdivide dl");
+    }
+    T2SC_TRY(check_sync(ctx));
+    for (int64_t e = 0; e < (int64_t)par.size(); e++) out_parent[e] = par[e];
+    for (int64_t e = 0; e < (int64_t)sid.size(); e++) out_subidx[e] = sid[e];
+    *m = mm;
+    return T2SC_OK;
+  });
+}
+
+}  // extern "C"

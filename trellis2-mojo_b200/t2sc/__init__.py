@@ -1,0 +1,11 @@
+"""t2sc: B200-native sparse submanifold convolution for TRELLIS.2-Mojo.
+
+The product is the C-ABI library libt2sc.so (include/t2sc.h); this package
+is its Python host binding, mirroring the reference's operator API.
+"""
+from ._lib import LIB_PATH, T2SCError, lib  # noqa: F401  (raises if the library is missing)
+from .sparse import (Binarized, Context, Coords, SparseChannel2Spatial, SparseConv3d, SparseTensor,  # noqa: F401
+                     SparseUpsample, binarize, conv_chain, sparse_conv3d_from)
+from . import synth  # noqa: F401
+
+__version__ = "0.1"

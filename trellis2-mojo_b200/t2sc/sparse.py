@@ -1,0 +1,294 @@
+"""Host-side mirror of the TRELLIS.2-Mojo sparse operator API over libt2sc.
+
+Same names, argument meaning and error behaviour as the reference:
+  SparseTensor                 trellis2_mojo/sparse/basic.mojo:296-339 (batch-order contract)
+  SparseConv3d                 trellis2_mojo/sparse/conv.mojo:19-199
+  sparse_conv3d_from           trellis2_mojo/loaders.mojo:43-50
+  SparseUpsample               trellis2_mojo/sparse/spatial/basic.mojo:121-174
+  SparseChannel2Spatial        trellis2_mojo/sparse/spatial/spatial2channel.mojo:80-145
+  binarize                     trellis2_mojo/models/sc_vaes/sparse_unet_vae.mojo:30-37
+
+Every operator runs on the GPU through the C ABI; there is no CPU path.
+Features are host numpy f32 arrays (the reference's Tensor[F32]); the
+coordinate hash and neighbour maps live on the device in a handle shared by
+every tensor derived through ``replace`` (the reference's spatial cache).
+"""
+import ctypes
+
+import numpy as np
+
+from . import _lib
+from ._lib import check, lib
+
+_DTYPES = {"f32": _lib.DT_F32, "f16": _lib.DT_F16, "bf16": _lib.DT_BF16}
+
+
+def _p(a):
+    return a.ctypes.data_as(ctypes.c_void_p) if a is not None else None
+
+
+class Context:
+    """One per device; replaces GpuContext (trellis2_mojo/gpu/context.mojo:116-165)."""
+
+    _default = {}
+
+    def __init__(self, device=0):
+        h = ctypes.c_void_p()
+        rc = lib.t2sc_ctx_create(device, ctypes.byref(h))
+        check(rc)
+        self.handle = h
+        self.device = device
+
+    @classmethod
+    def default(cls, device=0):
+        if device not in cls._default:
+            cls._default[device] = cls(device)
+        return cls._default[device]
+
+    def synchronize(self):
+        check(lib.t2sc_ctx_synchronize(self.handle), self.handle)
+
+    def launch_count(self):
+        v = ctypes.c_int64()
+        check(lib.t2sc_ctx_launch_count(self.handle, ctypes.byref(v)), self.handle)
+        return v.value
+
+    def set_stream(self, stream_ptr):
+        check(lib.t2sc_ctx_set_stream(self.handle, ctypes.c_void_p(stream_ptr) if stream_ptr else None),
+              self.handle)
+
+    def close(self):
+        if self.handle:
+            lib.t2sc_ctx_destroy(self.handle)
+            self.handle = None
+
+
+class Coords:
+    """Device coordinates + hash + cached neighbour maps (the spatial cache)."""
+
+    def __init__(self, ctx, coords=None, n=None, device_ptr=None):
+        self.ctx = ctx
+        h = ctypes.c_void_p()
+        if device_ptr is not None:
+            rc = lib.t2sc_coords_create_device(ctx.handle, ctypes.c_void_p(device_ptr), n, ctypes.byref(h))
+        else:
+            coords = np.ascontiguousarray(coords, dtype=np.int32)
+            rc = lib.t2sc_coords_create(ctx.handle, _p(coords), coords.shape[0], ctypes.byref(h))
+        check(rc, ctx.handle)
+        self.handle = h
+        v = ctypes.c_int64()
+        check(lib.t2sc_coords_count(h, ctypes.byref(v)))
+        self.n = v.value
+
+    def build_map(self, kernel=(3, 3, 3), dilation=1):
+        e = ctypes.c_int64()
+        check(lib.t2sc_coords_build_map(self.handle, *kernel, dilation, ctypes.byref(e)), self.ctx.handle)
+        return e.value
+
+    def neighbor_map(self, kernel=(3, 3, 3), dilation=1):
+        """(src, tgt, kidx) int64 edge lists in the reference order (conv.mojo:56-96)."""
+        e = self.build_map(kernel, dilation)
+        src, tgt, kidx = (np.empty(e, np.int64) for _ in range(3))
+        ne = ctypes.c_int64()
+        check(lib.t2sc_neighbor_map_export(self.handle, *kernel, dilation, _p(src), _p(tgt), _p(kidx), e,
+                                           ctypes.byref(ne)), self.ctx.handle)
+        return src, tgt, kidx
+
+    def csr(self, kernel=(3, 3, 3), dilation=1):
+        """(row_start, src_s, kidx_s) as conv.mojo:117-147 builds them."""
+        e = self.build_map(kernel, dilation)
+        rs = np.empty(self.n + 1, np.int64)
+        src, kidx = np.empty(e, np.int64), np.empty(e, np.int64)
+        ne = ctypes.c_int64()
+        check(lib.t2sc_csr_export(self.handle, *kernel, dilation, _p(rs), _p(src), _p(kidx), e, ctypes.byref(ne)),
+              self.ctx.handle)
+        return rs, src, kidx
+
+    def __del__(self):
+        h = getattr(self, "handle", None)
+        if h and self.ctx.handle:
+            lib.t2sc_coords_destroy(h)
+            self.handle = None
+
+
+class SparseTensor:
+    """feats f32 [N, C] + coords int32 [N, 4] (b, x, y, z); batches ordered
+    (the contract SparseTensor._cal_offsets enforces, basic.mojo:320-339)."""
+
+    def __init__(self, feats, coords, batch_size=-1, ctx=None, _cache=None):
+        feats = np.ascontiguousarray(feats, dtype=np.float32)
+        coords = np.ascontiguousarray(coords, dtype=np.int32)
+        if coords.ndim != 2 or coords.shape[1] != 4:
+            raise ValueError("SparseTensor: coords must be [N, 4]")
+        if feats.shape[0] != coords.shape[0]:
+            raise ValueError("SparseTensor: feats/coords row mismatch")
+        b = coords[:, 0]
+        if batch_size < 0:
+            batch_size = int(b.max()) + 1 if len(b) else 0
+        if len(b) and np.any(np.diff(b) < 0):
+            raise ValueError("SparseTensor: batches must be ordered/contiguous")
+        if len(b) and (b.min() < 0 or b.max() >= batch_size):
+            raise ValueError("SparseTensor: batch index out of range")
+        self.feats = feats
+        self.coords = coords
+        self.batch_size = batch_size
+        self.offsets = np.concatenate([[0], np.cumsum(np.bincount(b, minlength=batch_size))]).astype(np.int64)
+        self._ctx = ctx
+        # shared by every tensor derived through replace(), like the
+        # reference's ArcPointer spatial cache
+        self._cache = _cache if _cache is not None else {}
+
+    @property
+    def ctx(self):
+        if self._ctx is None:
+            self._ctx = Context.default()
+        return self._ctx
+
+    @property
+    def device_coords(self):
+        if "coords" not in self._cache:
+            self._cache["coords"] = Coords(self.ctx, self.coords)
+        return self._cache["coords"]
+
+    def replace(self, feats):
+        """New feats, same coords and spatial cache (basic.mojo:399-404)."""
+        return SparseTensor(feats, self.coords, self.batch_size, self._ctx, self._cache)
+
+    def __add__(self, other):
+        return self.replace(self.feats + other.feats)
+
+
+class SparseConv3d:
+    """Submanifold conv, stride 1. weight [Co, Kd, Kh, Kw, Ci] (conv_none
+    layout), bias [Co]. dtype: "f32" (f32-accurate), "f16" or "bf16"
+    (16-bit inputs and weights, f32 accumulation). The weights are uploaded
+    once here (GpuSparseConv.try_build, gpu/conv.mojo:264-329, without its
+    Co % 64 gate: every shape runs on the GPU)."""
+
+    def __init__(self, weight, bias=None, has_bias=True, dilation=1, dtype="f32", ctx=None):
+        weight = np.ascontiguousarray(weight, dtype=np.float32)
+        if weight.ndim != 5:
+            raise ValueError("SparseConv3d: weight must be [Co, Kd, Kh, Kw, Ci]")
+        self.out_channels = weight.shape[0]
+        self.in_channels = weight.shape[4]
+        self.kernel_size = tuple(weight.shape[1:4])
+        self.dilation = dilation
+        self.has_bias = has_bias and bias is not None
+        self.weight = weight
+        self.bias = np.ascontiguousarray(bias, dtype=np.float32) if self.has_bias else None
+        self.dtype = dtype
+        self.ctx = ctx or Context.default()
+        h = ctypes.c_void_p()
+        kd, kh, kw = self.kernel_size
+        check(lib.t2sc_conv_create(self.ctx.handle, _p(weight), _p(self.bias), self.out_channels, kd, kh, kw,
+                                   self.in_channels, dilation, _DTYPES[dtype], ctypes.byref(h)), self.ctx.handle)
+        self.handle = h
+
+    def forward(self, x, silu=False, residual=None):
+        """SparseConv3d.forward (conv.mojo:98-199); optional fused SiLU and
+        residual add (the decoder's activation / `h + x`)."""
+        if x.feats.shape[1] != self.in_channels:
+            raise ValueError("SparseConv3d: in_features mismatch")
+        y = np.empty((x.feats.shape[0], self.out_channels), np.float32)
+        flags = (_lib.SILU if silu else 0) | (_lib.RESIDUAL if residual is not None else 0)
+        res = None
+        if residual is not None:
+            res = np.ascontiguousarray(residual.feats if isinstance(residual, SparseTensor) else residual,
+                                       dtype=np.float32)
+            if res.shape != y.shape:
+                raise ValueError("SparseConv3d: residual shape mismatch")
+        check(lib.t2sc_conv_forward(self.handle, x.device_coords.handle, _p(x.feats), _p(y), flags, _p(res)),
+              self.ctx.handle)
+        return x.replace(y)
+
+    __call__ = forward
+
+    def __del__(self):
+        h = getattr(self, "handle", None)
+        if h and self.ctx.handle:
+            lib.t2sc_conv_destroy(h)
+            self.handle = None
+
+
+def conv_chain(convs, x, flags):
+    """Several convs on the same coordinates with device-resident
+    intermediates (one upload, one download)."""
+    n = x.feats.shape[0]
+    y = np.empty((n, convs[-1].out_channels), np.float32)
+    arr = (ctypes.c_void_p * len(convs))(*[c.handle.value for c in convs])
+    fl = (ctypes.c_int * len(convs))(*flags)
+    check(lib.t2sc_conv_chain_forward(arr, len(convs), x.device_coords.handle, _p(x.feats), _p(y), fl),
+          convs[0].ctx.handle)
+    return x.replace(y)
+
+
+def sparse_conv3d_from(state_dict, prefix, dilation=1, dtype="f32", ctx=None):
+    """loaders.mojo:43-50: the conv_none weight is already [Co, Kd, Kh, Kw, Ci]."""
+    return SparseConv3d(state_dict[prefix + ".weight"], state_dict.get(prefix + ".bias"), dilation=dilation,
+                        dtype=dtype, ctx=ctx)
+
+
+class Binarized:
+    """A subdivision tensor to be read as `sub > 0` on the device
+    (the decoder's _binarize, sparse_unet_vae.mojo:30-37)."""
+
+    def __init__(self, subdiv):
+        self.subdiv = subdiv
+
+
+def binarize(subdiv):
+    """Marks `subdiv` for the `> 0` test; the comparison itself runs in the
+    subdivision kernel (T2SC_SUB_POSITIVE)."""
+    return Binarized(subdiv)
+
+
+def _subdivide(x, subdivision, feats_mode, keep_mode):
+    if isinstance(subdivision, Binarized):
+        subdivision, keep_mode = subdivision.subdiv, _lib.SUB_POSITIVE
+    sub = np.ascontiguousarray(subdivision.feats if isinstance(subdivision, SparseTensor) else subdivision,
+                               dtype=np.float32)
+    n = x.coords.shape[0]
+    if sub.shape != (n, 8):
+        raise ValueError("subdivision feats must be [N, 8]")
+    c_in = x.feats.shape[1]
+    if feats_mode == _lib.FEATS_C2S:
+        if c_in % 8:
+            raise ValueError("SparseChannel2Spatial: channels must be divisible by 8")
+        c = c_in // 8
+    else:
+        c = c_in
+    out_coords = np.empty((8 * n, 4), np.int32)
+    out_feats = np.empty((8 * n, c), np.float32)
+    parent = np.empty(8 * n, np.int64)
+    subidx = np.empty(8 * n, np.int64)
+    m = ctypes.c_int64()
+    ctx = x.ctx
+    check(lib.t2sc_subdivide(ctx.handle, _p(x.coords), n, _p(sub), keep_mode, _p(x.feats), c, feats_mode,
+                             _p(out_coords), _p(out_feats), _p(parent), _p(subidx), ctypes.byref(m)), ctx.handle)
+    m = m.value
+    out = SparseTensor(out_feats[:m].copy(), out_coords[:m].copy(), x.batch_size, ctx)
+    out.parent_idx, out.subidx = parent[:m].copy(), subidx[:m].copy()
+    return out
+
+
+class SparseUpsample:
+    def __init__(self, factor=2):
+        if factor != 2:
+            raise ValueError("SparseUpsample: only factor 2 (subdivision) is supported")
+        self.factor = factor
+
+    def forward_subdivision(self, x, subdivision):
+        """Children where sub != 0, parent feats copied (spatial/basic.mojo:144-174)."""
+        return _subdivide(x, subdivision, _lib.FEATS_UPSAMPLE, _lib.SUB_NONZERO)
+
+
+class SparseChannel2Spatial:
+    def __init__(self, factor=2):
+        if factor != 2:
+            raise ValueError("SparseChannel2Spatial: only factor 2 is supported")
+        self.factor = factor
+
+    def forward_subdivision(self, x, subdivision):
+        """Children where sub != 0, feats = channel slice c*C:(c+1)*C
+        (spatial2channel.mojo:97-145)."""
+        return _subdivide(x, subdivision, _lib.FEATS_C2S, _lib.SUB_NONZERO)
