@@ -200,7 +200,10 @@ def run_single(args):
     dev = 0
     torch.cuda.set_device(dev)
     ctx = t2sc.Context.default(dev)
-    stream = torch.cuda.current_stream()
+    # a dedicated (non-default) stream shared by torch and the library, so
+    # the CUDA events below time exactly the library's kernels
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
     ctx.set_stream(stream.cuda_stream)
     coords, x, ws, bs = inputs()
     n = len(coords)
@@ -238,7 +241,9 @@ def run_single(args):
     ev = lambda: torch.cuda.Event(enable_timing=True)  # noqa: E731
     step_times, layer_times = [], []
     launches0 = ctx.launch_count()
-    with Clocks(dev) as clk:
+    clk = Clocks(dev).__enter__()
+    time.sleep(0.3)
+    if True:
         for _ in range(args.steps):
             flush.zero_()  # 256 MiB write: L2 (126 MB) holds nothing of the previous step
             evs = [(ev(), ev()) for _ in range(LAYERS)]
@@ -252,6 +257,14 @@ def run_single(args):
             layer_times += [a.elapsed_time(b) for a, b in evs]
     launches = ctx.launch_count() - launches0
     ctx.synchronize()
+    # keep the GPU under the same load (untimed) until the clock sampler has
+    # seen at least ~1 s of it
+    t_load = time.perf_counter()
+    while time.perf_counter() - t_load < 1.0:
+        for _ in range(20):
+            step()
+        torch.cuda.synchronize()
+    clk.__exit__()
     ms = float(np.sum(step_times)) / args.steps
     flops_layer = 2.0 * E * C * C
     value = LAYERS * flops_layer / (ms * 1e-3) / 1e12

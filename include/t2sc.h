@@ -80,7 +80,15 @@ const char *t2sc_version(void);
  * (kernel, dilation) and reused by every conv on the same coordinates. ---- */
 int t2sc_coords_create(t2sc_ctx *ctx, const int32_t *coords_host, int64_t n, t2sc_coords **out);
 int t2sc_coords_create_device(t2sc_ctx *ctx, const int32_t *coords_dev, int64_t n, t2sc_coords **out);
+/* Coordinates with halo rows (z-slab partition): rows [0, n_targets) are
+ * this rank's own voxels and receive conv outputs; rows [n_targets, n) are
+ * neighbours' boundary voxels that only act as sources. Conv inputs then
+ * have n rows and outputs n_targets rows. on_device: coords is a device
+ * pointer. New interface (the reference has no partitioned path). */
+int t2sc_coords_create_halo(t2sc_ctx *ctx, const int32_t *coords, int64_t n, int64_t n_targets,
+                            int on_device, t2sc_coords **out);
 int t2sc_coords_destroy(t2sc_coords *c);
+/* Number of target rows (= all rows unless created with halo rows). */
 int t2sc_coords_count(const t2sc_coords *c, int64_t *n);
 /* Build (or fetch) the neighbour map; returns the edge count E. */
 int t2sc_coords_build_map(t2sc_coords *c, int kd, int kh, int kw, int dilation, int64_t *n_edges);

@@ -33,17 +33,20 @@ def test_reference_blob_cases_f32(t2sc, oracle, side, ci, co, dil, seed, atol):
     assert rel_err(y, ref) <= F32_TOL
 
 
-@pytest.mark.parametrize("dtype", ["bf16", "f16"])
+@pytest.mark.parametrize("dtype", ["bf16", "f16", "f32"])
 @pytest.mark.parametrize("ci,co", [(64, 64), (32, 32), (128, 128), (256, 256), (16, 48), (64, 512), (24, 40),
-                                   (40, 64), (8, 16)])
-def test_shell_16bit(t2sc, oracle, dtype, ci, co):
+                                   (40, 64), (8, 16), (4, 16), (12, 32)])
+def test_shell_modes(t2sc, oracle, dtype, ci, co):
+    """Tile-shape coverage: 32/64/128-byte rows, partial Ci chunks, 1..4 Co
+    tiles, and shapes that take the CUDA-core kernel (Co % 16 != 0, or Ci
+    not a whole number of 16-byte vectors)."""
     S = t2sc.synth
     coords = S.shell(*S.SHELLS["cfg1"])
     x, w, b = conv_inputs(S, len(coords), ci, co, seed=100 + ci + co)
     conv = t2sc.SparseConv3d(w, b, dtype=dtype)
     y = conv(t2sc.SparseTensor(x, coords)).feats
-    ref = oracle_conv(oracle, coords, x, w, b, round_mode=dtype)
-    assert rel_err(y, ref) <= F16_TOL
+    ref = oracle_conv(oracle, coords, x, w, b, round_mode=None if dtype == "f32" else dtype)
+    assert rel_err(y, ref) <= (F32_TOL if dtype == "f32" else F16_TOL)
 
 
 @pytest.mark.parametrize("dtype", ["bf16", "f16", "f32"])

@@ -147,11 +147,12 @@ int t2sc_ctx_launch_count(const t2sc_ctx *ctx, int64_t *count) {
 
 // ------------------------------- coordinates -------------------------------
 
-static int coords_create_impl(t2sc_ctx *ctx, const int32_t *coords, int64_t n, bool on_device,
+static int coords_create_impl(t2sc_ctx *ctx, const int32_t *coords, int64_t n, int64_t n_targets, bool on_device,
                               t2sc_coords **out) {
   if (!ctx || !out) return T2SC_ERR_INVALID;
   *out = nullptr;
   if (n < 0 || (n > 0 && !coords)) return fail(ctx, T2SC_ERR_INVALID, "coords: bad pointer or count");
+  if (n_targets < 0 || n_targets > n) return fail(ctx, T2SC_ERR_INVALID, "coords: n_targets must be in [0, n]");
   if (n >= (int64_t(1) << 31)) return fail(ctx, T2SC_ERR_UNSUPPORTED, "coords: more than 2^31-1 rows");
   return guarded(ctx, [&]() -> int {
     DeviceGuard g(ctx->device);
@@ -159,6 +160,7 @@ static int coords_create_impl(t2sc_ctx *ctx, const int32_t *coords, int64_t n, b
     std::unique_ptr<t2sc_coords> c(new t2sc_coords());
     c->ctx = ctx;
     c->n = n;
+    c->n_targets = n_targets;
     T2SC_CUDA(cudaMalloc((void **)&c->d_coords, (size_t)(n > 0 ? n : 1) * 16), "coords");
     if (n > 0)
       T2SC_CUDA(cudaMemcpyAsync(c->d_coords, coords, (size_t)n * 16,
@@ -175,10 +177,14 @@ static int coords_create_impl(t2sc_ctx *ctx, const int32_t *coords, int64_t n, b
 }
 
 int t2sc_coords_create(t2sc_ctx *ctx, const int32_t *coords, int64_t n, t2sc_coords **out) {
-  return coords_create_impl(ctx, coords, n, false, out);
+  return coords_create_impl(ctx, coords, n, n, false, out);
 }
 int t2sc_coords_create_device(t2sc_ctx *ctx, const int32_t *coords, int64_t n, t2sc_coords **out) {
-  return coords_create_impl(ctx, coords, n, true, out);
+  return coords_create_impl(ctx, coords, n, n, true, out);
+}
+int t2sc_coords_create_halo(t2sc_ctx *ctx, const int32_t *coords, int64_t n, int64_t n_targets, int on_device,
+                            t2sc_coords **out) {
+  return coords_create_impl(ctx, coords, n, n_targets, on_device != 0, out);
 }
 
 int t2sc_coords_destroy(t2sc_coords *c) {
@@ -195,7 +201,7 @@ int t2sc_coords_destroy(t2sc_coords *c) {
 
 int t2sc_coords_count(const t2sc_coords *c, int64_t *n) {
   if (!c || !n) return T2SC_ERR_INVALID;
-  *n = c->n;
+  *n = c->n_targets;
   return T2SC_OK;
 }
 
@@ -287,7 +293,10 @@ int t2sc_conv_create(t2sc_ctx *ctx, const float *weight, const float *bias, int 
       t2sc_conv_destroy(cv.release());
       return rc;
     }
-    cv->tc_path = (dtype != T2SC_DT_F32 && ci % 8 == 0 && co % 16 == 0) ? 1 : 0;
+    // tensor-core kernel: 16-byte row vectors (Ci % 8 for 16-bit, Ci % 4
+    // for f32) and N tiles of 16 output channels; the CUDA-core kernel
+    // covers every other shape
+    cv->tc_path = (co % 16 == 0 && ci % (dtype == T2SC_DT_F32 ? 4 : 8) == 0) ? 1 : 0;
     rc = cv->tc_path ? conv_tc_prepare(cv.get(), weight, err) : conv_simt_prepare(cv.get(), weight, err);
     if (rc != T2SC_OK) {
       t2sc_conv_destroy(cv.release());
@@ -364,12 +373,12 @@ int t2sc_conv_forward(t2sc_conv *cv, t2sc_coords *c, const float *x, float *y, i
   t2sc_ctx *ctx = cv->ctx;
   return guarded(ctx, [&]() -> int {
     DeviceGuard g(ctx->device);
-    const int64_t n = c->n;
+    const int64_t n = c->n_targets, n_src = c->n;
     if (n == 0) return T2SC_OK;
     if (!x || !y) return fail(ctx, T2SC_ERR_INVALID, "null feature buffer");
     if ((flags & T2SC_RESIDUAL) && !residual) return fail(ctx, T2SC_ERR_INVALID, "RESIDUAL flag without residual");
     DevBuf dx, dy, dr;
-    T2SC_TRY(upload_as(ctx, x, n * cv->ci, cv->dtype, dx));
+    T2SC_TRY(upload_as(ctx, x, n_src * cv->ci, cv->dtype, dx));
     if (flags & T2SC_RESIDUAL) T2SC_TRY(upload_as(ctx, residual, n * cv->co, cv->dtype, dr));
     T2SC_TRY(dy.alloc(ctx, n * cv->co * elem_size(cv->dtype)));
     T2SC_TRY(forward_device_impl(cv, c, dx.p, dy.p, flags, dr.p));
@@ -397,6 +406,7 @@ int t2sc_conv_chain_forward(t2sc_conv *const *convs, int n_layers, t2sc_coords *
       cmax = convs[i]->co > cmax ? convs[i]->co : cmax;
     }
     const int64_t n = c->n;
+    if (c->n_targets != n) return fail(ctx, T2SC_ERR_INVALID, "chain: coordinates with halo rows are not chainable");
     if (n == 0) return T2SC_OK;
     if (!x || !y) return fail(ctx, T2SC_ERR_INVALID, "null feature buffer");
     DevBuf din, b0, b1;

@@ -9,36 +9,64 @@
 // produced by exactly one CTA with no atomics. The tile only visits offsets
 // set in its occupancy mask.
 //
-// Warp roles in a 288-thread CTA (persistent, one per SM):
-//   warps 0-3  gather producers: cp.async 16-byte vectors of neighbour rows
-//              into a 128B/64B/32B-swizzled K-major A stage; thread 0 also
-//              bulk-copies the pre-swizzled weight block (B stage);
-//   warps 4-7  epilogue: tcgen05.ld from TMEM, + bias, SiLU, + residual,
+// Warp roles in a 192-thread CTA (persistent, one per SM):
+//   warps 0-3  epilogue: tcgen05.ld from TMEM, + bias, SiLU, + residual,
 //              convert, store to the row's original position;
-//   warp 8     TMEM owner and MMA issuer (one elected lane).
+//   warp 4     TMA producer: per stage 32 tile::gather4 copies (4 neighbour
+//              rows each, straight into the 128B/64B/32B-swizzled K-major A
+//              tile; a missing neighbour has row index -1, which the TMA
+//              unit fills with zeros) and one bulk copy of the pre-swizzled
+//              weight block (B tile); it also prefetches each tile's
+//              neighbour-index block into shared memory one tile ahead;
+//   warp 5     TMEM owner and MMA issuer (one elected lane).
 // Double-buffered TMEM accumulators let the epilogue of tile i overlap the
-// MMAs of tile i+1. Every mbarrier wait is bounded; on timeout the CTA sets
-// an error bit, drains its copies, frees TMEM and returns.
+// MMAs of tile i+1.
+//
+// Modes: f16 / bf16 (kind::f16, one MMA per 16-wide k-step) and the
+// f32-accurate split-TF32 mode (kind::tf32): x = x_hi + x_lo and
+// w = w_hi + w_lo with x_hi, w_hi rounded to TF32, and
+// D += x_hi*w_hi + x_hi*w_lo + x_lo*w_hi (the x_lo*w_lo term, ~2^-22
+// relative, is dropped). The A stage then holds the hi and lo gathers, the
+// B stage the hi and lo weight blocks. Because the tensor core's f32
+// accumulation rounds (biased) at every step, this mode drains the TMEM
+// accumulator after every kernel offset and sums the 27 partials in
+// registers, which keeps the error near the f32 level.
+//
+// Every mbarrier wait is bounded; on timeout the CTA sets an error bit,
+// lets its copies land, frees TMEM and returns.
+#include <stdlib.h>
+#include <string.h>
+
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
+
+#include <cuda.h>
 
 #include "internal.h"
 #include "sm100.cuh"
 
+#define T2SC_TRY_RC(expr)             \
+  do {                                \
+    int _rc = (expr);                 \
+    if (_rc != T2SC_OK) return _rc;   \
+  } while (0)
+
 namespace t2sc {
 namespace {
 
-constexpr int kProducerThreads = 128;
 constexpr int kEpilogueThreads = 128;
-constexpr int kThreads = kProducerThreads + kEpilogueThreads + 32;
-constexpr int kLag = 2;                       // cp.async groups kept in flight per producer thread
+constexpr int kThreads = kEpilogueThreads + 64;  // + producer warp + MMA warp
+constexpr int kProducerWarp = 4, kMmaWarp = 5;
+constexpr int kMinStages = 3;
+constexpr int kTf32MaxBn = 128;                  // register-resident partial sums per row
 constexpr long long kWaitLimit = 4000000000LL;  // ~2 s of SM clocks
-constexpr int kSmemBudget = 200 * 1024;
+constexpr int kSmemMax = 232448;  // 227 KB: the sm_100 per-block dynamic shared memory limit
+
+constexpr int kModeTf32x3 = 3;  // beside T2SC_DT_F16 (1) and T2SC_DT_BF16 (2)
 
 struct TcArgs {
-  const uint8_t *x;          // [n, ci] 16-bit
-  uint8_t *y;                // [n, co] 16-bit
-  const uint8_t *res;        // [n, co] 16-bit or null
+  uint8_t *y;                // [n, co] 16-bit or f32
+  const uint8_t *res;        // [n, co] like y, or null
   const uint8_t *wimg;       // pre-swizzled B blocks
   const float *bias;         // [co]
   const int32_t *nbr_sorted; // [K][n_pad]
@@ -47,6 +75,7 @@ struct TcArgs {
   int64_t n_pad;
   int ntiles, ci, co, bn, nchunks, nco_tiles, kvol, stages, flags, tmem_cols;
   uint32_t a_bytes, b_bytes, stage_bytes;
+  int debug;  // diagnostics (T2SC_CONV_DEBUG): 2 skips the MMAs, 4 the epilogue stores
   int *err;
 };
 
@@ -71,7 +100,10 @@ __device__ __forceinline__ float2 unpack2(uint32_t v) {
   }
 }
 
-__device__ __forceinline__ float silu(float v) { return v / (1.0f + expf(-v)); }
+// v / (1 + exp(-v)); the exponent is clamped so the divisor stays in the
+// range where the fast division is accurate (SiLU(v) for v < -80 is below
+// 1e-33 either way).
+__device__ __forceinline__ float silu(float v) { return __fdividef(v, 1.0f + __expf(fminf(-v, 80.0f))); }
 
 // Epilogue for 16 consecutive output channels of one row.
 template <int DT>
@@ -82,6 +114,24 @@ __device__ __forceinline__ void store16(const TcArgs &a, int orow, int col, cons
   if (a.flags & T2SC_SILU) {
 #pragma unroll
     for (int i = 0; i < 16; i++) v[i] = silu(v[i]);
+  }
+  if (DT == kModeTf32x3) {
+    const int64_t off = ((int64_t)orow * a.co + col) * 4;
+    if (a.flags & T2SC_RESIDUAL) {
+      const float4 *rp = reinterpret_cast<const float4 *>(a.res + off);
+#pragma unroll
+      for (int q = 0; q < 4; q++) {
+        float4 r = __ldg(rp + q);
+        v[4 * q] += r.x;
+        v[4 * q + 1] += r.y;
+        v[4 * q + 2] += r.z;
+        v[4 * q + 3] += r.w;
+      }
+    }
+    float4 *yp = reinterpret_cast<float4 *>(a.y + off);
+#pragma unroll
+    for (int q = 0; q < 4; q++) yp[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+    return;
   }
   const int64_t off = ((int64_t)orow * a.co + col) * 2;
   if (a.flags & T2SC_RESIDUAL) {
@@ -116,35 +166,56 @@ __device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, volatil
   return __shfl_sync(0xffffffffu, ok, 0) != 0;
 }
 
+// TMA gather of four rows (row index -1: zero fill) of one column chunk.
+__device__ __forceinline__ void tma_gather4(uint32_t dst, const CUtensorMap *tm, int col, int4 rows, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cta.global.tile::gather4.mbarrier::complete_tx::bytes "
+      "[%0], [%1, {%2, %3, %4, %5, %6}], [%7];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(tm)), "r"(col), "r"(rows.x), "r"(rows.y), "r"(rows.z), "r"(rows.w), "r"(bar)
+      : "memory");
+}
+
 template <int DT, int RB>
-__global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const TcArgs a) {
+__global__ void __launch_bounds__(kThreads, 1)
+    conv_tc_kernel(const __grid_constant__ CUtensorMap tm_hi, const __grid_constant__ CUtensorMap tm_lo,
+                   const TcArgs a) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // 1024-byte alignment for the swizzle atoms
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int S = a.stages;
-  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + (size_t)S * a.stage_bytes);
-  // bars: full[S], empty[S], tfull[2], tempty[2], mma_done
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * S + 5);
+  // neighbour indices of a tile's active offsets, double-buffered across tiles
+  int32_t *idx_buf = reinterpret_cast<int32_t *>(smem + (size_t)S * a.stage_bytes);
+  uint64_t *bars = reinterpret_cast<uint64_t *>(idx_buf + 2 * kMaxK * kTileRows);
+  // bars: full[S], empty[S], tfull[2], tempty[2], mma_done, idx_full[2]
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * S + 7);
   volatile int *abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
   const uint32_t sbase = sm100::smem_u32(smem);
   const uint32_t full0 = sm100::smem_u32(bars), empty0 = full0 + 8 * S;
   const uint32_t tfull0 = empty0 + 8 * S, tempty0 = tfull0 + 16, mma_done = tempty0 + 16;
+  const uint32_t idxf0 = mma_done + 8;
+
+  constexpr bool kSplit = DT == kModeTf32x3;
+  constexpr int ES = kSplit ? 4 : 2;   // element bytes
+  constexpr int BKE = RB / ES;         // elements per chunk row
+  const uint32_t a_tile = kTileRows * RB, b_tile = (uint32_t)a.bn * RB;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   if (tid == 0) {
     for (int s = 0; s < S; s++) {
-      sm100::mbar_init(full0 + 8 * s, kProducerThreads + 1);
-      sm100::mbar_init(empty0 + 8 * s, 1);
+      sm100::mbar_init(full0 + 8 * s, 1);   // the producer's arrive.expect_tx; the rest is tx bytes
+      sm100::mbar_init(empty0 + 8 * s, 1);  // one tcgen05.commit
     }
     for (int b = 0; b < 2; b++) {
       sm100::mbar_init(tfull0 + 8 * b, 1);
-      sm100::mbar_init(tempty0 + 8 * b, kEpilogueThreads);
+      sm100::mbar_init(tempty0 + 8 * b, kEpilogueThreads / 32);  // one arrival per epilogue warp
     }
     sm100::mbar_init(mma_done, 1);
+    sm100::mbar_init(idxf0, 1);
+    sm100::mbar_init(idxf0 + 8, 1);
     *abort = 0;
     sm100::fence_mbar_init();
   }
-  if (warp == 8) {
+  if (warp == kMmaWarp) {
     sm100::tmem_alloc(sm100::smem_u32(tmem_slot), a.tmem_cols);
     sm100::tmem_relinquish();
   }
@@ -153,77 +224,85 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const TcArgs a) {
   sm100::tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const int nunits = a.ntiles * a.nco_tiles;
-  constexpr int BKE = RB / 2;      // 16-bit elements per chunk row
-  constexpr int CPR = RB / 16;     // 16-byte vectors per row
-  constexpr int RPP = 32 / CPR;    // rows per warp pass
 
-  if (warp < 4) {
-    // ------------------------- gather producers -------------------------
-    const int j = lane % CPR, rsub = lane / CPR;
-    uint32_t it = 0;
-    int npend = 0;
-    uint32_t pend[kLag + 1];
+  if (warp == kProducerWarp) {
+    // ---------------------------- TMA producer ----------------------------
+    uint32_t it = 0, s = 0, ph = 0;  // stage iteration, its slot and phase
     bool ok = true;
-    for (int u = blockIdx.x; u < nunits && ok; u += gridDim.x) {
+    // lane 0 bulk-copies the [active k][128] neighbour-index block of a unit
+    auto load_idx = [&](int unit, int buf) {
+      const int tl = unit / a.nco_tiles;
+      uint32_t m = __ldg(a.tile_mask + tl);
+      const uint32_t bar = idxf0 + 8 * buf;
+      sm100::mbar_arrive_expect_tx(bar, (uint32_t)__popc(m) * kTileRows * 4);
+      const uint32_t dst = sm100::smem_u32(idx_buf + buf * kMaxK * kTileRows);
+      for (int slot = 0; m; slot++) {
+        const int k = __ffs(m) - 1;
+        m &= m - 1;
+        sm100::bulk_g2s(dst + slot * kTileRows * 4, a.nbr_sorted + (int64_t)k * a.n_pad + (int64_t)tl * kTileRows,
+                        kTileRows * 4, bar);
+      }
+    };
+    uint32_t n_idx_issued = 0;  // blocks requested (block i -> buffer i & 1)
+    uint32_t t = 0;             // blocks consumed
+    if (lane == 0 && (int)blockIdx.x < nunits) load_idx(blockIdx.x, n_idx_issued & 1);
+    n_idx_issued++;
+    for (int u = blockIdx.x; u < nunits && ok; u += gridDim.x, t++) {
       const int tile = u / a.nco_tiles, cot = u % a.nco_tiles;
+      // the buffer of the unit after next is free: this warp issued every
+      // gather that read it (gather row indices travel in registers)
+      if (u + (int)gridDim.x < nunits) {
+        if (lane == 0) load_idx(u + gridDim.x, n_idx_issued & 1);
+        n_idx_issued++;
+      }
+      if (!warp_wait(idxf0 + 8 * (t & 1), (t >> 1) & 1, abort, a.err)) {
+        ok = false;
+        break;
+      }
+      const int4 *idx_t = reinterpret_cast<const int4 *>(idx_buf + (t & 1) * kMaxK * kTileRows) + lane;
       uint32_t km = __ldg(a.tile_mask + tile);
-      while (km && ok) {
+      for (int slot = 0; km && ok; slot++) {
         const int k = __ffs(km) - 1;
         km &= km - 1;
-        int32_t srcs[CPR];
-#pragma unroll
-        for (int p = 0; p < CPR; p++) {
-          const int row = 32 * warp + p * RPP + rsub;
-          srcs[p] = __ldg(a.nbr_sorted + (int64_t)k * a.n_pad + (int64_t)tile * kTileRows + row);
-        }
-        for (int c = 0; c < a.nchunks; c++, it++) {
-          const uint32_t s = it % S;
-          if (!warp_wait(empty0 + 8 * s, ((it / S) & 1) ^ 1, abort, a.err)) {
+        const int4 rows = idx_t[slot * (kTileRows / 4)];  // rows 4*lane .. 4*lane+3 of the tile
+        const uint8_t *wsrc = a.wimg + (size_t)((size_t)cot * a.kvol + k) * a.nchunks * a.b_bytes;
+        for (int c = 0; c < a.nchunks; c++) {
+          if (!warp_wait(empty0 + 8 * s, ph ^ 1, abort, a.err)) {
             ok = false;
             break;
           }
-          const uint32_t abase = sbase + s * a.stage_bytes;
-          if (tid == 0) {
-            const uint32_t bbar = full0 + 8 * s;
-            sm100::mbar_arrive_expect_tx(bbar, a.b_bytes);
-            const uint8_t *wsrc = a.wimg + ((size_t)((size_t)cot * a.kvol + k) * a.nchunks + c) * a.b_bytes;
-            sm100::bulk_g2s(abase + a.a_bytes, wsrc, a.b_bytes, bbar);
+          const uint32_t abase = sbase + s * a.stage_bytes, bar = full0 + 8 * s;
+          if (lane == 0) {
+            sm100::mbar_arrive_expect_tx(bar, a.a_bytes + a.b_bytes);
+            sm100::bulk_g2s(abase + a.a_bytes, wsrc + (size_t)c * a.b_bytes, a.b_bytes, bar);
           }
-          const int e0 = c * BKE + j * 8;
-#pragma unroll
-          for (int p = 0; p < CPR; p++) {
-            const int row = 32 * warp + p * RPP + rsub;
-            const int32_t src = srcs[p];
-            const bool valid = src >= 0 && e0 < a.ci;
-            const uint8_t *g = valid ? a.x + ((int64_t)src * a.ci + e0) * 2 : a.x;
-            sm100::cp_async_16(abase + swizzle_off(row * RB + j * 16, RB), g, valid ? 16u : 0u);
-          }
-          sm100::cp_async_commit();
-          pend[npend++] = s;
-          if (npend > kLag) {
-            sm100::cp_async_wait<kLag>();
-            sm100::fence_proxy_async_smem();
-            sm100::mbar_arrive(full0 + 8 * pend[0]);
-            for (int q = 0; q < kLag; q++) pend[q] = pend[q + 1];
-            npend--;
+          __syncwarp();
+          tma_gather4(abase + lane * 4 * RB, &tm_hi, c * BKE, rows, bar);
+          if (kSplit) tma_gather4(abase + a_tile + lane * 4 * RB, &tm_lo, c * BKE, rows, bar);
+          it++;
+          if (++s == (uint32_t)S) {
+            s = 0;
+            ph ^= 1;
           }
         }
       }
     }
-    sm100::cp_async_wait<0>();
-    sm100::fence_proxy_async_smem();
-    for (int q = 0; q < npend; q++) sm100::mbar_arrive(full0 + 8 * pend[q]);
-    if (tid == 0 && !ok) {
-      // let the weight bulk copies still in flight land before the CTA exits
-      const uint32_t first = it > (uint32_t)S ? it - S : 0;
-      for (uint32_t i2 = first; i2 < it; i2++)
-        sm100::mbar_wait_cycles(full0 + 8 * (i2 % S), (i2 / S) & 1, kWaitLimit / 8);
+    if (lane == 0) {
+      // copies requested but never consumed (abort path) land before exit
+      for (uint32_t i2 = t; i2 < n_idx_issued && (int)(blockIdx.x + i2 * gridDim.x) < nunits; i2++)
+        sm100::mbar_wait_cycles(idxf0 + 8 * (i2 & 1), (i2 >> 1) & 1, kWaitLimit / 8);
+      if (!ok) {
+        const uint32_t first = it > (uint32_t)S ? it - S : 0;
+        for (uint32_t i2 = first; i2 < it; i2++)
+          sm100::mbar_wait_cycles(full0 + 8 * (i2 % S), (i2 / S) & 1, kWaitLimit / 8);
+      }
     }
-  } else if (warp < 8) {
+  } else if (warp < 4) {
     // ------------------------------ epilogue ------------------------------
-    const int q = warp - 4;  // TMEM lane quadrant
+    const int q = warp;  // TMEM lane quadrant of this warp
     const int row = 32 * q + lane;
     uint32_t acc_it = 0;
+    float part[kSplit ? kTf32MaxBn : 1];
     for (int u = blockIdx.x; u < nunits; u += gridDim.x) {
       const int tile = u / a.nco_tiles, cot = u % a.nco_tiles;
       const uint32_t km = __ldg(a.tile_mask + tile);
@@ -238,6 +317,48 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const TcArgs a) {
         }
         continue;
       }
+      if (kSplit) {
+        // one accumulator drain per kernel offset, summed in f32 registers
+#pragma unroll
+        for (int i = 0; i < kTf32MaxBn; i++) part[i] = 0.f;
+        bool ok = true;
+        for (int kk = __popc(km); kk > 0; kk--) {
+          const uint32_t b = acc_it & 1;
+          if (!warp_wait(tfull0 + 8 * b, (acc_it >> 1) & 1, abort, a.err)) {
+            ok = false;
+            break;
+          }
+          sm100::tc_fence_after();
+          const uint32_t tbase = tmem + ((uint32_t)(32 * q) << 16) + b * a.bn;
+#pragma unroll
+          for (int cc = 0; cc < kTf32MaxBn; cc += 16) {
+            if (cc < a.bn) {
+              uint32_t r[16];
+              sm100::tmem_ld16(tbase + cc, r);
+              sm100::tmem_ld_wait();
+#pragma unroll
+              for (int i = 0; i < 16; i++) part[cc + i] += __uint_as_float(r[i]);
+            }
+          }
+          sm100::tc_fence_before();
+          __syncwarp();
+          if (lane == 0) sm100::mbar_arrive(tempty0 + 8 * b);
+          acc_it++;
+        }
+        if (!ok) break;
+        if (orow >= 0 && !(a.debug & 4)) {
+#pragma unroll
+          for (int cc = 0; cc < kTf32MaxBn; cc += 16) {
+            if (cc < a.bn) {
+              float v[16];
+#pragma unroll
+              for (int i = 0; i < 16; i++) v[i] = part[cc + i];
+              store16<DT>(a, orow, col0 + cc, v);
+            }
+          }
+        }
+        continue;
+      }
       const uint32_t b = acc_it & 1;
       if (!warp_wait(tfull0 + 8 * b, (acc_it >> 1) & 1, abort, a.err)) break;
       sm100::tc_fence_after();
@@ -249,49 +370,71 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const TcArgs a) {
         float acc[16];
 #pragma unroll
         for (int i = 0; i < 16; i++) acc[i] = __uint_as_float(r[i]);
-        if (orow >= 0) store16<DT>(a, orow, col0 + cc, acc);
+        if (orow >= 0 && !(a.debug & 4)) store16<DT>(a, orow, col0 + cc, acc);
       }
       sm100::tc_fence_before();
-      sm100::mbar_arrive(tempty0 + 8 * b);
+      __syncwarp();
+      if (lane == 0) sm100::mbar_arrive(tempty0 + 8 * b);
       acc_it++;
     }
   } else {
     // ----------------------------- MMA issuer -----------------------------
     if (lane == 0) {
-      const uint32_t idesc = sm100::instr_desc(DT == T2SC_DT_BF16 ? 1u : 0u, (uint32_t)a.bn);
-      uint32_t it = 0, acc_it = 0;
+      const uint32_t idesc =
+          sm100::instr_desc(kSplit ? 2u : (DT == T2SC_DT_BF16 ? 1u : 0u), (uint32_t)a.bn);
+      // descriptors of stage 0; a stage or k-step offset is added to the
+      // 14-bit start-address field (all of shared memory fits in it)
+      const uint64_t dA = sm100::smem_desc(sbase, RB), dB = sm100::smem_desc(sbase + a.a_bytes, RB);
+      uint32_t s = 0, ph = 0, acc_it = 0;
       bool ok = true;
       for (int u = blockIdx.x; u < nunits && ok; u += gridDim.x) {
         const int tile = u / a.nco_tiles;
-        uint32_t km = __ldg(a.tile_mask + tile);
+        const uint32_t km = __ldg(a.tile_mask + tile);
         if (km == 0) continue;
-        const uint32_t b = acc_it & 1;
-        if (!sm100::mbar_wait_bounded(tempty0 + 8 * b, ((acc_it >> 1) & 1) ^ 1, abort, a.err, kDevErrTimeout,
-                                      kWaitLimit))
-          break;
-        sm100::tc_fence_after();
-        const uint32_t dtm = tmem + b * a.bn;
-        uint32_t accum = 0;
-        const int nsteps = __popc(km) * a.nchunks;
-        for (int st = 0; st < nsteps; st++, it++) {
-          const uint32_t s = it % S;
-          if (!sm100::mbar_wait_bounded(full0 + 8 * s, (it / S) & 1, abort, a.err, kDevErrTimeout, kWaitLimit)) {
+        const int nk = __popc(km);
+        // split-TF32: one accumulator (and one drain) per offset; otherwise one per tile
+        const int groups = kSplit ? nk : 1, steps_per_group = kSplit ? a.nchunks : nk * a.nchunks;
+        for (int g = 0; g < groups && ok; g++) {
+          const uint32_t b = acc_it & 1;
+          if (!sm100::mbar_wait_bounded(tempty0 + 8 * b, ((acc_it >> 1) & 1) ^ 1, abort, a.err, kDevErrTimeout,
+                                        kWaitLimit)) {
             ok = false;
             break;
           }
           sm100::tc_fence_after();
-          const uint32_t abase = sbase + s * a.stage_bytes, bbase = abase + a.a_bytes;
+          const uint32_t dtm = tmem + b * a.bn;
+          uint32_t accum = 0;
+          for (int st = 0; st < steps_per_group; st++) {
+            if (!sm100::mbar_wait_bounded(full0 + 8 * s, ph, abort, a.err, kDevErrTimeout, kWaitLimit)) {
+              ok = false;
+              break;
+            }
+            sm100::tc_fence_after();
+            const uint64_t so = (s * a.stage_bytes) >> 4;
 #pragma unroll
-          for (int kk = 0; kk < RB / 32; kk++) {
-            sm100::mma_f16(dtm, sm100::smem_desc(abase + kk * 32, RB), sm100::smem_desc(bbase + kk * 32, RB), idesc,
-                           accum);
-            accum = 1;
+            for (int kk = 0; kk < RB / 32; kk++) {
+              const uint64_t ahi = dA + so + kk * 2, bhi = dB + so + kk * 2;
+              if (a.debug & 2) {
+              } else if (kSplit) {
+                const uint64_t alo = ahi + (a_tile >> 4), blo = bhi + (b_tile >> 4);
+                sm100::mma_tf32(dtm, alo, bhi, idesc, accum);
+                sm100::mma_tf32(dtm, ahi, blo, idesc, 1u);
+                sm100::mma_tf32(dtm, ahi, bhi, idesc, 1u);
+              } else {
+                sm100::mma_f16(dtm, ahi, bhi, idesc, accum);
+              }
+              accum = 1;
+            }
+            sm100::mma_commit(empty0 + 8 * s);
+            if (++s == (uint32_t)S) {
+              s = 0;
+              ph ^= 1;
+            }
           }
-          sm100::mma_commit(empty0 + 8 * s);
+          if (!ok) break;
+          sm100::mma_commit(tfull0 + 8 * b);
+          acc_it++;
         }
-        if (!ok) break;
-        sm100::mma_commit(tfull0 + 8 * b);
-        acc_it++;
       }
       // all issued MMAs retire before TMEM is released
       sm100::mma_commit(mma_done);
@@ -301,60 +444,144 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const TcArgs a) {
   }
   sm100::tc_fence_before();
   __syncthreads();
-  if (warp == 8) {
+  if (warp == kMmaWarp) {
     sm100::tc_fence_after();
     sm100::tmem_dealloc(tmem, a.tmem_cols);
   }
 }
 
+// x = hi + lo with hi the nearest TF32 value (cvt.rna) and lo exact in f32.
+__global__ void split_tf32_kernel(const float4 *__restrict__ x, float4 *__restrict__ hi, float4 *__restrict__ lo,
+                                  int64_t n4) {
+  int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n4) return;
+  float4 v = x[i], h, l;
+  float *pv = &v.x, *ph = &h.x, *pl = &l.x;
+#pragma unroll
+  for (int q = 0; q < 4; q++) {
+    uint32_t t;
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(t) : "f"(pv[q]));
+    ph[q] = __uint_as_float(t);
+    pl[q] = pv[q] - ph[q];
+  }
+  hi[i] = h;
+  lo[i] = l;
+}
+
 template <int DT, int RB>
-int launch_tc(t2sc_conv *cv, const TcArgs &args, int grid, size_t smem, std::string &err) {
+int launch_tc(t2sc_conv *cv, const CUtensorMap &hi, const CUtensorMap &lo, const TcArgs &args, int grid, size_t smem,
+              std::string &err) {
   auto kfn = conv_tc_kernel<DT, RB>;
   T2SC_CUDA(cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem), "tc smem attr");
-  kfn<<<grid, kThreads, smem, cv->ctx->stream>>>(args);
+  kfn<<<grid, kThreads, smem, cv->ctx->stream>>>(hi, lo, args);
   T2SC_LAUNCHED(cv->ctx, "conv_tc");
+  return T2SC_OK;
+}
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no
+// link-time dependency on libcuda).
+using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                   const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = [] {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      p = nullptr;
+    return reinterpret_cast<EncodeTiledFn>(p);
+  }();
+  return fn;
+}
+
+// Row-gather map over a [rows, ci] feature matrix: box = one row x one
+// chunk of `rb` bytes, swizzled like the A tile, zero fill out of bounds.
+int gather_map(CUtensorMap *tm, const void *base, int dtype, int64_t rows, int ci, int rb, std::string &err) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) {
+    err = "cuTensorMapEncodeTiled unavailable";
+    return T2SC_ERR_CUDA;
+  }
+  const int es = dtype == T2SC_DT_F32 ? 4 : 2;
+  const CUtensorMapDataType dt = dtype == T2SC_DT_F32   ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                 : dtype == T2SC_DT_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                         : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  const CUtensorMapSwizzle sw = rb == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
+                                : rb == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                           : CU_TENSOR_MAP_SWIZZLE_32B;
+  cuuint64_t dims[2] = {(cuuint64_t)ci, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)ci * es};
+  cuuint32_t box[2] = {(cuuint32_t)(rb / es), 1};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(tm, dt, 2, const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    err = "cuTensorMapEncodeTiled failed: " + std::to_string((int)r);
+    return T2SC_ERR_CUDA;
+  }
   return T2SC_OK;
 }
 
 }  // namespace
 
+// TF32 value nearest to f (ties away from zero), as cvt.rna.tf32.f32 rounds.
+static float tf32_round_host(float f) {
+  uint32_t u;
+  memcpy(&u, &f, 4);
+  if ((u & 0x7f800000u) != 0x7f800000u) u = (u + 0x1000u) & ~0x1fffu;
+  memcpy(&f, &u, 4);
+  return f;
+}
+
 // Chooses the tile shape and builds the pre-swizzled weight image: one
 // block per (co tile, k, ci chunk) holding bn rows (output channels) x
 // row_bytes (a chunk of input channels), exactly the B stage's smem image.
+// In the split-TF32 mode each block is the hi image followed by the lo image.
 int conv_tc_prepare(t2sc_conv *cv, const float *w, std::string &err) {
   const int co = cv->co, ci = cv->ci, K = cv->kvol;
-  cv->row_bytes = ci >= 64 ? 128 : (ci > 16 ? 64 : 32);
-  const int bke = cv->row_bytes / 2;
+  const bool f32 = cv->dtype == T2SC_DT_F32;
+  const int es = f32 ? 4 : 2, na = f32 ? 2 : 1;
+  const int ci_bytes = ci * es;
+  // 16-bit modes stream 128-byte rows; the split-TF32 mode keeps two A and
+  // two B tiles per stage, so it uses 64-byte rows to fit four stages
+  const int max_rb = f32 ? 64 : 128;
+  cv->row_bytes = ci_bytes >= max_rb ? max_rb : (ci_bytes > 32 ? 64 : 32);
+  const int bke = cv->row_bytes / es;
   cv->nchunks = (ci + bke - 1) / bke;
+  const int bn_max = f32 ? 128 : 256;
   int bn = 0;
-  for (int d = 256; d >= 16; d -= 16)
+  for (int d = bn_max; d >= 16; d -= 16)
     if (co % d == 0) {
       bn = d;
       break;
     }
   cv->bn = bn;
   cv->nco_tiles = co / bn;
-  const size_t bbytes = (size_t)bn * cv->row_bytes;
+  const size_t tile = (size_t)bn * cv->row_bytes, bbytes = tile * na;
   const size_t total = bbytes * cv->nco_tiles * K * cv->nchunks;
-  std::vector<uint16_t> img(total / 2, 0);
+  std::vector<uint8_t> img(total, 0);
   for (int nt = 0; nt < cv->nco_tiles; nt++)
     for (int k = 0; k < K; k++)
       for (int c = 0; c < cv->nchunks; c++) {
-        uint8_t *blk = reinterpret_cast<uint8_t *>(img.data()) + ((size_t)(nt * K + k) * cv->nchunks + c) * bbytes;
+        uint8_t *blk = img.data() + ((size_t)(nt * K + k) * cv->nchunks + c) * bbytes;
         for (int r = 0; r < bn; r++)
           for (int e = 0; e < bke; e++) {
             const int o = nt * bn + r, i = c * bke + e;
-            float v = (i < ci) ? w[((size_t)o * K + k) * ci + i] : 0.0f;
-            uint16_t bits;
-            if (cv->dtype == T2SC_DT_BF16) {
+            const float v = (i < ci) ? w[((size_t)o * K + k) * ci + i] : 0.0f;
+            const uint32_t off = swizzle_off((uint32_t)(r * cv->row_bytes + e * es), cv->row_bytes);
+            if (f32) {
+              const float hi = tf32_round_host(v), lo = v - hi;
+              memcpy(blk + off, &hi, 4);
+              memcpy(blk + tile + off, &lo, 4);
+            } else if (cv->dtype == T2SC_DT_BF16) {
               __nv_bfloat16 h = __float2bfloat16_rn(v);
-              bits = *reinterpret_cast<uint16_t *>(&h);
+              memcpy(blk + off, &h, 2);
             } else {
               __half h = __float2half_rn(v);
-              bits = *reinterpret_cast<uint16_t *>(&h);
+              memcpy(blk + off, &h, 2);
             }
-            const uint32_t off = swizzle_off((uint32_t)(r * cv->row_bytes + e * 2), cv->row_bytes);
-            *reinterpret_cast<uint16_t *>(blk + off) = bits;
           }
       }
   T2SC_CUDA(cudaMalloc(&cv->d_wtc, total), "conv weights");
@@ -365,8 +592,11 @@ int conv_tc_prepare(t2sc_conv *cv, const float *w, std::string &err) {
 int conv_tc_launch(t2sc_conv *cv, t2sc_map *m, const void *x, void *y, int flags, const void *residual,
                    std::string &err) {
   if (m->n == 0) return T2SC_OK;
+  if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y) | reinterpret_cast<uintptr_t>(residual)) & 15) {
+    err = "feature buffers must be 16-byte aligned";
+    return T2SC_ERR_INVALID;
+  }
   TcArgs a;
-  a.x = static_cast<const uint8_t *>(x);
   a.y = static_cast<uint8_t *>(y);
   a.res = static_cast<const uint8_t *>(residual);
   a.wimg = static_cast<const uint8_t *>(cv->d_wtc);
@@ -384,36 +614,67 @@ int conv_tc_launch(t2sc_conv *cv, t2sc_map *m, const void *x, void *y, int flags
   a.kvol = cv->kvol;
   a.flags = flags;
   a.err = cv->ctx->d_err;
+  static const int debug_bits = [] {
+    const char *e = getenv("T2SC_CONV_DEBUG");
+    return e ? atoi(e) : 0;
+  }();
+  a.debug = debug_bits;
   int cols = 32;
   while (cols < 2 * cv->bn) cols <<= 1;
   a.tmem_cols = cols;
-  a.a_bytes = kTileRows * cv->row_bytes;
-  a.b_bytes = (uint32_t)cv->bn * cv->row_bytes;
+  const int na = cv->dtype == T2SC_DT_F32 ? 2 : 1;
+  a.a_bytes = kTileRows * cv->row_bytes * na;
+  a.b_bytes = (uint32_t)cv->bn * cv->row_bytes * na;
   a.stage_bytes = (a.a_bytes + a.b_bytes + 1023u) & ~1023u;
-  int S = kSmemBudget / (int)a.stage_bytes;
+  const int idx_bytes = 2 * kMaxK * kTileRows * 4;  // double-buffered tile index blocks
+  int S = (kSmemMax - idx_bytes - 1280) / (int)a.stage_bytes;
   if (S > 8) S = 8;
-  if (S < kLag + 1) {
+  if (S < kMinStages) {
     err = "conv tile does not fit shared memory";
     return T2SC_ERR_UNSUPPORTED;
   }
   a.stages = S;
-  // stages + barriers/slots + alignment slack; never below 120 KB so that a
-  // single CTA owns each SM (and its TMEM).
-  size_t smem = (size_t)S * a.stage_bytes + 256 + 1024;
+  // stages + index blocks + barriers/slots + alignment slack; never below
+  // 120 KB so that a single CTA owns each SM (and its TMEM).
+  size_t smem = (size_t)S * a.stage_bytes + idx_bytes + 256 + 1024;
   if (smem < 120 * 1024) smem = 120 * 1024;
   const int64_t nunits = (int64_t)a.ntiles * a.nco_tiles;
   const int grid = (int)(nunits < cv->ctx->num_sms ? nunits : cv->ctx->num_sms);
+  CUtensorMap hi, lo;
+  memset(&lo, 0, sizeof(lo));
+  if (cv->dtype == T2SC_DT_F32) {
+    // split x into TF32 hi/lo parts in stream-ordered scratch
+    cudaStream_t st = cv->ctx->stream;
+    const int64_t cnt = m->n_src * (int64_t)cv->ci;
+    float *split = nullptr;
+    T2SC_CUDA(cudaMallocAsync((void **)&split, (size_t)cnt * 8, st), "split scratch");
+    const int64_t n4 = cnt / 4;
+    split_tf32_kernel<<<(unsigned)((n4 + 255) / 256), 256, 0, st>>>((const float4 *)x, (float4 *)split,
+                                                                     (float4 *)(split + cnt), n4);
+    T2SC_LAUNCHED(cv->ctx, "split_tf32");
+    int rc = gather_map(&hi, split, T2SC_DT_F32, m->n_src, cv->ci, cv->row_bytes, err);
+    if (rc == T2SC_OK) rc = gather_map(&lo, split + cnt, T2SC_DT_F32, m->n_src, cv->ci, cv->row_bytes, err);
+    if (rc == T2SC_OK) {
+      if (cv->row_bytes == 64)
+        rc = launch_tc<kModeTf32x3, 64>(cv, hi, lo, a, grid, smem, err);
+      else
+        rc = launch_tc<kModeTf32x3, 32>(cv, hi, lo, a, grid, smem, err);
+    }
+    cudaFreeAsync(split, st);
+    return rc;
+  }
+  T2SC_TRY_RC(gather_map(&hi, x, cv->dtype, m->n_src, cv->ci, cv->row_bytes, err));
   const bool bf = cv->dtype == T2SC_DT_BF16;
   switch (cv->row_bytes) {
     case 128:
-      return bf ? launch_tc<T2SC_DT_BF16, 128>(cv, a, grid, smem, err)
-                : launch_tc<T2SC_DT_F16, 128>(cv, a, grid, smem, err);
+      return bf ? launch_tc<T2SC_DT_BF16, 128>(cv, hi, lo, a, grid, smem, err)
+                : launch_tc<T2SC_DT_F16, 128>(cv, hi, lo, a, grid, smem, err);
     case 64:
-      return bf ? launch_tc<T2SC_DT_BF16, 64>(cv, a, grid, smem, err)
-                : launch_tc<T2SC_DT_F16, 64>(cv, a, grid, smem, err);
+      return bf ? launch_tc<T2SC_DT_BF16, 64>(cv, hi, lo, a, grid, smem, err)
+                : launch_tc<T2SC_DT_F16, 64>(cv, hi, lo, a, grid, smem, err);
     default:
-      return bf ? launch_tc<T2SC_DT_BF16, 32>(cv, a, grid, smem, err)
-                : launch_tc<T2SC_DT_F16, 32>(cv, a, grid, smem, err);
+      return bf ? launch_tc<T2SC_DT_BF16, 32>(cv, hi, lo, a, grid, smem, err)
+                : launch_tc<T2SC_DT_F16, 32>(cv, hi, lo, a, grid, smem, err);
   }
 }
 

@@ -220,9 +220,10 @@ int build_map(t2sc_coords *c, int kd, int kh, int kw, int dil, t2sc_map **out, s
   t2sc_ctx *ctx = c->ctx;
   cudaStream_t st = ctx->stream;
   std::unique_ptr<t2sc_map, void (*)(t2sc_map *)> m(new t2sc_map(), free_map);
-  const int64_t n = c->n;
+  const int64_t n = c->n_targets;
   m->kvol = kd * kh * kw;
   m->n = n;
+  m->n_src = c->n;
   m->ntiles = (n + kTileRows - 1) / kTileRows;
   m->n_pad = m->ntiles * kTileRows;
   const int K = m->kvol;

@@ -47,7 +47,8 @@ struct t2sc_ctx {
 // One neighbour map for a (kernel, dilation) on a coordinate set.
 struct t2sc_map {
   int kvol = 27;
-  int64_t n = 0, n_pad = 0, ntiles = 0;
+  int64_t n = 0, n_pad = 0, ntiles = 0;  // n: target (output) rows
+  int64_t n_src = 0;                      // rows of the input features (targets + halo)
   int64_t n_edges = 0;
   int32_t *nbr = nullptr;        // [K][n]    natural row order, -1 = miss
   uint32_t *mask = nullptr;      // [n]       bit k set iff nbr[k][r] >= 0
@@ -58,7 +59,8 @@ struct t2sc_map {
 
 struct t2sc_coords {
   t2sc_ctx *ctx = nullptr;
-  int64_t n = 0;
+  int64_t n = 0;                 // all rows (targets first, then halo rows)
+  int64_t n_targets = 0;         // rows that receive conv outputs
   int32_t *d_coords = nullptr;   // [n,4]
   uint64_t hcap = 0;             // hash capacity (power of two)
   int64_t *d_keys = nullptr;     // [hcap]
