@@ -9,16 +9,17 @@
 // produced by exactly one CTA with no atomics. The tile only visits offsets
 // set in its occupancy mask.
 //
-// Warp roles in a 192-thread CTA (persistent, one per SM):
+// Warp roles in a 288-thread CTA (persistent, one per SM):
 //   warps 0-3  epilogue: tcgen05.ld from TMEM, + bias, SiLU, + residual,
 //              convert, store to the row's original position;
-//   warp 4     TMA producer: per stage 32 tile::gather4 copies (4 neighbour
-//              rows each, straight into the 128B/64B/32B-swizzled K-major A
-//              tile; a missing neighbour has row index -1, which the TMA
-//              unit fills with zeros) and one bulk copy of the pre-swizzled
-//              weight block (B tile); it also prefetches each tile's
-//              neighbour-index block into shared memory one tile ahead;
-//   warp 5     TMEM owner and MMA issuer (one elected lane).
+//   warps 4-7  gather producers: 16-byte cp.async vectors of the neighbour
+//              rows straight into the 128B/64B/32B-swizzled K-major A tile
+//              (zero-filled for a missing neighbour); each thread publishes
+//              its copies with cp.async.mbarrier.arrive.noinc, so up to S
+//              stages are in flight. Thread 0 of the group also bulk-copies
+//              the pre-swizzled weight block (B tile) and prefetches each
+//              tile's neighbour-index block into shared memory a tile ahead;
+//   warp 8     TMEM owner and MMA issuer (one elected lane).
 // Double-buffered TMEM accumulators let the epilogue of tile i overlap the
 // MMAs of tile i+1.
 //
@@ -40,23 +41,16 @@
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
-#include <cuda.h>
-
 #include "internal.h"
 #include "sm100.cuh"
-
-#define T2SC_TRY_RC(expr)             \
-  do {                                \
-    int _rc = (expr);                 \
-    if (_rc != T2SC_OK) return _rc;   \
-  } while (0)
 
 namespace t2sc {
 namespace {
 
 constexpr int kEpilogueThreads = 128;
-constexpr int kThreads = kEpilogueThreads + 64;  // + producer warp + MMA warp
-constexpr int kProducerWarp = 4, kMmaWarp = 5;
+constexpr int kProducerThreads = 128;
+constexpr int kThreads = kEpilogueThreads + kProducerThreads + 32;  // + MMA warp
+constexpr int kProducerWarp0 = 4, kMmaWarp = 8;
 constexpr int kMinStages = 3;
 constexpr int kTf32MaxBn = 128;                  // register-resident partial sums per row
 constexpr long long kWaitLimit = 4000000000LL;  // ~2 s of SM clocks
@@ -65,6 +59,8 @@ constexpr int kSmemMax = 232448;  // 227 KB: the sm_100 per-block dynamic shared
 constexpr int kModeTf32x3 = 3;  // beside T2SC_DT_F16 (1) and T2SC_DT_BF16 (2)
 
 struct TcArgs {
+  const uint8_t *x;          // [n_src, ci] 16-bit, or the f32 hi parts (split-TF32 mode)
+  const uint8_t *x_lo;       // [n_src, ci] f32 lo parts (split-TF32 mode)
   uint8_t *y;                // [n, co] 16-bit or f32
   const uint8_t *res;        // [n, co] like y, or null
   const uint8_t *wimg;       // pre-swizzled B blocks
@@ -166,19 +162,9 @@ __device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, volatil
   return __shfl_sync(0xffffffffu, ok, 0) != 0;
 }
 
-// TMA gather of four rows (row index -1: zero fill) of one column chunk.
-__device__ __forceinline__ void tma_gather4(uint32_t dst, const CUtensorMap *tm, int col, int4 rows, uint32_t bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cta.global.tile::gather4.mbarrier::complete_tx::bytes "
-      "[%0], [%1, {%2, %3, %4, %5, %6}], [%7];" ::"r"(dst),
-      "l"(reinterpret_cast<uint64_t>(tm)), "r"(col), "r"(rows.x), "r"(rows.y), "r"(rows.z), "r"(rows.w), "r"(bar)
-      : "memory");
-}
-
 template <int DT, int RB>
 __global__ void __launch_bounds__(kThreads, 1)
-    conv_tc_kernel(const __grid_constant__ CUtensorMap tm_hi, const __grid_constant__ CUtensorMap tm_lo,
-                   const TcArgs a) {
+    conv_tc_kernel(const TcArgs a) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // 1024-byte alignment for the swizzle atoms
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -202,7 +188,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   if (tid == 0) {
     for (int s = 0; s < S; s++) {
-      sm100::mbar_init(full0 + 8 * s, 1);   // the producer's arrive.expect_tx; the rest is tx bytes
+      // one cp.async completion arrival per producer thread + the weight copy's expect_tx
+      sm100::mbar_init(full0 + 8 * s, kProducerThreads + 1);
       sm100::mbar_init(empty0 + 8 * s, 1);  // one tcgen05.commit
     }
     for (int b = 0; b < 2; b++) {
@@ -225,11 +212,23 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem = *tmem_slot;
   const int nunits = a.ntiles * a.nco_tiles;
 
-  if (warp == kProducerWarp) {
-    // ---------------------------- TMA producer ----------------------------
+  if (warp >= kProducerWarp0 && warp < kMmaWarp) {
+    // --------------------------- gather producers ---------------------------
+    // Lane (rsub, j) of producer warp w copies 16-byte vector j of tile rows
+    // 32w + p*RPP + rsub (p < CPR); its swizzled smem offsets are fixed.
+    constexpr int CPR = RB / 16;   // 16-byte vectors per row
+    constexpr int RPP = 32 / CPR;  // rows per warp pass
+    constexpr int EPV = 16 / ES;   // elements per vector
+    const int pw = warp - kProducerWarp0, ptid = tid - 32 * kProducerWarp0;
+    const int j = lane % CPR, rsub = lane / CPR;
+    uint32_t soff[CPR];
+#pragma unroll
+    for (int p = 0; p < CPR; p++) soff[p] = swizzle_off((32 * pw + p * RPP + rsub) * RB + j * 16, RB);
+    const int64_t row_stride = (int64_t)a.ci * ES;
+    const int64_t lo_delta = kSplit ? (a.x_lo - a.x) : 0;
     uint32_t it = 0, s = 0, ph = 0;  // stage iteration, its slot and phase
     bool ok = true;
-    // lane 0 bulk-copies the [active k][128] neighbour-index block of a unit
+    // thread 0 bulk-copies the [active k][128] neighbour-index block of a unit
     auto load_idx = [&](int unit, int buf) {
       const int tl = unit / a.nco_tiles;
       uint32_t m = __ldg(a.tile_mask + tl);
@@ -245,26 +244,34 @@ __global__ void __launch_bounds__(kThreads, 1)
     };
     uint32_t n_idx_issued = 0;  // blocks requested (block i -> buffer i & 1)
     uint32_t t = 0;             // blocks consumed
-    if (lane == 0 && (int)blockIdx.x < nunits) load_idx(blockIdx.x, n_idx_issued & 1);
+    if (ptid == 0) load_idx(blockIdx.x, 0);
     n_idx_issued++;
     for (int u = blockIdx.x; u < nunits && ok; u += gridDim.x, t++) {
       const int tile = u / a.nco_tiles, cot = u % a.nco_tiles;
-      // the buffer of the unit after next is free: this warp issued every
-      // gather that read it (gather row indices travel in registers)
+      // every producer thread is done reading the buffer the next prefetch overwrites
+      asm volatile("bar.sync 1, %0;" ::"n"(kProducerThreads) : "memory");
       if (u + (int)gridDim.x < nunits) {
-        if (lane == 0) load_idx(u + gridDim.x, n_idx_issued & 1);
+        if (ptid == 0) load_idx(u + gridDim.x, n_idx_issued & 1);
         n_idx_issued++;
       }
       if (!warp_wait(idxf0 + 8 * (t & 1), (t >> 1) & 1, abort, a.err)) {
         ok = false;
         break;
       }
-      const int4 *idx_t = reinterpret_cast<const int4 *>(idx_buf + (t & 1) * kMaxK * kTileRows) + lane;
+      const int32_t *idx_t = idx_buf + (t & 1) * kMaxK * kTileRows + 32 * pw + lane;
       uint32_t km = __ldg(a.tile_mask + tile);
       for (int slot = 0; km && ok; slot++) {
         const int k = __ffs(km) - 1;
         km &= km - 1;
-        const int4 rows = idx_t[slot * (kTileRows / 4)];  // rows 4*lane .. 4*lane+3 of the tile
+        const int32_t mysrc = idx_t[slot * kTileRows];
+        const uint8_t *gp[CPR];
+        uint32_t gs[CPR];
+#pragma unroll
+        for (int p = 0; p < CPR; p++) {
+          const int32_t src = __shfl_sync(0xffffffffu, mysrc, p * RPP + rsub);
+          gp[p] = a.x + (src >= 0 ? (int64_t)src * row_stride : 0) + j * 16;
+          gs[p] = src >= 0 ? 16u : 0u;
+        }
         const uint8_t *wsrc = a.wimg + (size_t)((size_t)cot * a.kvol + k) * a.nchunks * a.b_bytes;
         for (int c = 0; c < a.nchunks; c++) {
           if (!warp_wait(empty0 + 8 * s, ph ^ 1, abort, a.err)) {
@@ -272,13 +279,19 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           const uint32_t abase = sbase + s * a.stage_bytes, bar = full0 + 8 * s;
-          if (lane == 0) {
-            sm100::mbar_arrive_expect_tx(bar, a.a_bytes + a.b_bytes);
+          if (ptid == 0) {
+            sm100::mbar_arrive_expect_tx(bar, a.b_bytes);
             sm100::bulk_g2s(abase + a.a_bytes, wsrc + (size_t)c * a.b_bytes, a.b_bytes, bar);
           }
-          __syncwarp();
-          tma_gather4(abase + lane * 4 * RB, &tm_hi, c * BKE, rows, bar);
-          if (kSplit) tma_gather4(abase + a_tile + lane * 4 * RB, &tm_lo, c * BKE, rows, bar);
+          const bool cvalid = c * BKE + j * EPV < a.ci;
+#pragma unroll
+          for (int p = 0; p < CPR; p++) {
+            const uint32_t sz = cvalid ? gs[p] : 0u;
+            sm100::cp_async_16(abase + soff[p], gp[p] + c * RB, sz);
+            if (kSplit) sm100::cp_async_16(abase + a_tile + soff[p], gp[p] + lo_delta + c * RB, sz);
+          }
+          // arrives on the stage barrier once this thread's copies have landed
+          sm100::cp_async_arrive_noinc(bar);
           it++;
           if (++s == (uint32_t)S) {
             s = 0;
@@ -287,7 +300,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
-    if (lane == 0) {
+    sm100::cp_async_wait<0>();
+    if (ptid == 0) {
       // copies requested but never consumed (abort path) land before exit
       for (uint32_t i2 = t; i2 < n_idx_issued && (int)(blockIdx.x + i2 * gridDim.x) < nunits; i2++)
         sm100::mbar_wait_cycles(idxf0 + 8 * (i2 & 1), (i2 >> 1) & 1, kWaitLimit / 8);
@@ -469,58 +483,11 @@ __global__ void split_tf32_kernel(const float4 *__restrict__ x, float4 *__restri
 }
 
 template <int DT, int RB>
-int launch_tc(t2sc_conv *cv, const CUtensorMap &hi, const CUtensorMap &lo, const TcArgs &args, int grid, size_t smem,
-              std::string &err) {
+int launch_tc(t2sc_conv *cv, const TcArgs &args, int grid, size_t smem, std::string &err) {
   auto kfn = conv_tc_kernel<DT, RB>;
   T2SC_CUDA(cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem), "tc smem attr");
-  kfn<<<grid, kThreads, smem, cv->ctx->stream>>>(hi, lo, args);
+  kfn<<<grid, kThreads, smem, cv->ctx->stream>>>(args);
   T2SC_LAUNCHED(cv->ctx, "conv_tc");
-  return T2SC_OK;
-}
-
-// cuTensorMapEncodeTiled through the runtime's driver entry point (no
-// link-time dependency on libcuda).
-using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
-                                   const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
-                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-EncodeTiledFn encode_fn() {
-  static EncodeTiledFn fn = [] {
-    void *p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
-        q != cudaDriverEntryPointSuccess)
-      p = nullptr;
-    return reinterpret_cast<EncodeTiledFn>(p);
-  }();
-  return fn;
-}
-
-// Row-gather map over a [rows, ci] feature matrix: box = one row x one
-// chunk of `rb` bytes, swizzled like the A tile, zero fill out of bounds.
-int gather_map(CUtensorMap *tm, const void *base, int dtype, int64_t rows, int ci, int rb, std::string &err) {
-  EncodeTiledFn enc = encode_fn();
-  if (!enc) {
-    err = "cuTensorMapEncodeTiled unavailable";
-    return T2SC_ERR_CUDA;
-  }
-  const int es = dtype == T2SC_DT_F32 ? 4 : 2;
-  const CUtensorMapDataType dt = dtype == T2SC_DT_F32   ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
-                                 : dtype == T2SC_DT_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
-                                                         : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-  const CUtensorMapSwizzle sw = rb == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
-                                : rb == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
-                                           : CU_TENSOR_MAP_SWIZZLE_32B;
-  cuuint64_t dims[2] = {(cuuint64_t)ci, (cuuint64_t)rows};
-  cuuint64_t strides[1] = {(cuuint64_t)ci * es};
-  cuuint32_t box[2] = {(cuuint32_t)(rb / es), 1};
-  cuuint32_t estr[2] = {1, 1};
-  CUresult r = enc(tm, dt, 2, const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
-                   CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) {
-    err = "cuTensorMapEncodeTiled failed: " + std::to_string((int)r);
-    return T2SC_ERR_CUDA;
-  }
   return T2SC_OK;
 }
 
@@ -597,6 +564,8 @@ int conv_tc_launch(t2sc_conv *cv, t2sc_map *m, const void *x, void *y, int flags
     return T2SC_ERR_INVALID;
   }
   TcArgs a;
+  a.x = static_cast<const uint8_t *>(x);
+  a.x_lo = nullptr;
   a.y = static_cast<uint8_t *>(y);
   a.res = static_cast<const uint8_t *>(residual);
   a.wimg = static_cast<const uint8_t *>(cv->d_wtc);
@@ -640,8 +609,6 @@ int conv_tc_launch(t2sc_conv *cv, t2sc_map *m, const void *x, void *y, int flags
   if (smem < 120 * 1024) smem = 120 * 1024;
   const int64_t nunits = (int64_t)a.ntiles * a.nco_tiles;
   const int grid = (int)(nunits < cv->ctx->num_sms ? nunits : cv->ctx->num_sms);
-  CUtensorMap hi, lo;
-  memset(&lo, 0, sizeof(lo));
   if (cv->dtype == T2SC_DT_F32) {
     // split x into TF32 hi/lo parts in stream-ordered scratch
     cudaStream_t st = cv->ctx->stream;
@@ -652,29 +619,24 @@ int conv_tc_launch(t2sc_conv *cv, t2sc_map *m, const void *x, void *y, int flags
     split_tf32_kernel<<<(unsigned)((n4 + 255) / 256), 256, 0, st>>>((const float4 *)x, (float4 *)split,
                                                                      (float4 *)(split + cnt), n4);
     T2SC_LAUNCHED(cv->ctx, "split_tf32");
-    int rc = gather_map(&hi, split, T2SC_DT_F32, m->n_src, cv->ci, cv->row_bytes, err);
-    if (rc == T2SC_OK) rc = gather_map(&lo, split + cnt, T2SC_DT_F32, m->n_src, cv->ci, cv->row_bytes, err);
-    if (rc == T2SC_OK) {
-      if (cv->row_bytes == 64)
-        rc = launch_tc<kModeTf32x3, 64>(cv, hi, lo, a, grid, smem, err);
-      else
-        rc = launch_tc<kModeTf32x3, 32>(cv, hi, lo, a, grid, smem, err);
-    }
+    a.x = reinterpret_cast<const uint8_t *>(split);
+    a.x_lo = reinterpret_cast<const uint8_t *>(split + cnt);
+    int rc = cv->row_bytes == 64 ? launch_tc<kModeTf32x3, 64>(cv, a, grid, smem, err)
+                                 : launch_tc<kModeTf32x3, 32>(cv, a, grid, smem, err);
     cudaFreeAsync(split, st);
     return rc;
   }
-  T2SC_TRY_RC(gather_map(&hi, x, cv->dtype, m->n_src, cv->ci, cv->row_bytes, err));
   const bool bf = cv->dtype == T2SC_DT_BF16;
   switch (cv->row_bytes) {
     case 128:
-      return bf ? launch_tc<T2SC_DT_BF16, 128>(cv, hi, lo, a, grid, smem, err)
-                : launch_tc<T2SC_DT_F16, 128>(cv, hi, lo, a, grid, smem, err);
+      return bf ? launch_tc<T2SC_DT_BF16, 128>(cv, a, grid, smem, err)
+                : launch_tc<T2SC_DT_F16, 128>(cv, a, grid, smem, err);
     case 64:
-      return bf ? launch_tc<T2SC_DT_BF16, 64>(cv, hi, lo, a, grid, smem, err)
-                : launch_tc<T2SC_DT_F16, 64>(cv, hi, lo, a, grid, smem, err);
+      return bf ? launch_tc<T2SC_DT_BF16, 64>(cv, a, grid, smem, err)
+                : launch_tc<T2SC_DT_F16, 64>(cv, a, grid, smem, err);
     default:
-      return bf ? launch_tc<T2SC_DT_BF16, 32>(cv, hi, lo, a, grid, smem, err)
-                : launch_tc<T2SC_DT_F16, 32>(cv, hi, lo, a, grid, smem, err);
+      return bf ? launch_tc<T2SC_DT_BF16, 32>(cv, a, grid, smem, err)
+                : launch_tc<T2SC_DT_F16, 32>(cv, a, grid, smem, err);
   }
 }
 

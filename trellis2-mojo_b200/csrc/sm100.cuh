@@ -74,6 +74,11 @@ template <int N>
 __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
+// Arrive on the mbarrier when every cp.async this thread issued so far has
+// completed; .noinc: the arrival counts against the barrier's expected count.
+__device__ __forceinline__ void cp_async_arrive_noinc(uint32_t bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(bar) : "memory");
+}
 // Make generic-proxy shared-memory writes visible to the async proxy
 // (tcgen05.mma reads its operands through the async proxy).
 __device__ __forceinline__ void fence_proxy_async_smem() {
