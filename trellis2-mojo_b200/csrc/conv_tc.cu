@@ -35,6 +35,7 @@
 //
 // Every mbarrier wait is bounded; on timeout the CTA sets an error bit,
 // lets its copies land, frees TMEM and returns.
+#include <stdio.h>
 #include <stdlib.h>
 #include <string.h>
 
@@ -48,15 +49,22 @@ namespace t2sc {
 namespace {
 
 constexpr int kEpilogueThreads = 128;
-constexpr int kProducerThreads = 128;
-constexpr int kThreads = kEpilogueThreads + kProducerThreads + 32;  // + MMA warp
-constexpr int kProducerWarp0 = 4, kMmaWarp = 8;
 constexpr int kMinStages = 3;
 constexpr int kTf32MaxBn = 128;                  // register-resident partial sums per row
 constexpr long long kWaitLimit = 4000000000LL;  // ~2 s of SM clocks
 constexpr int kSmemMax = 232448;  // 227 KB: the sm_100 per-block dynamic shared memory limit
-
-constexpr int kModeTf32x3 = 3;  // beside T2SC_DT_F16 (1) and T2SC_DT_BF16 (2)
+constexpr int kModeTf32x3 = 3;    // beside T2SC_DT_F16 (1) and T2SC_DT_BF16 (2)
+constexpr int kCopyWarp0 = 4;
+// Warp roles: 0-3 epilogue; kCopyWarps copy warps (8 in the 16-bit modes,
+// 4 in the split-TF32 mode, whose epilogue needs the registers); one
+// control warp (weight copies, index prefetch); one MMA warp.
+template <int DT>
+struct Roles {
+  static constexpr int kCopyWarps = DT == 3 ? 4 : 8;
+  static constexpr int kControlWarp = kCopyWarp0 + kCopyWarps;
+  static constexpr int kMmaWarp = kControlWarp + 1;
+  static constexpr int kThreads = 32 * (kMmaWarp + 1);
+};
 
 struct TcArgs {
   const uint8_t *x;          // [n_src, ci] 16-bit, or the f32 hi parts (split-TF32 mode)
@@ -70,10 +78,17 @@ struct TcArgs {
   const uint32_t *tile_mask; // [ntiles]
   int64_t n_pad;
   int ntiles, ci, co, bn, nchunks, nco_tiles, kvol, stages, flags, tmem_cols;
-  uint32_t a_bytes, b_bytes, stage_bytes;
+  uint32_t a_bytes, b_bytes, sub_bytes, stage_bytes;  // per (k, chunk) pair: A, B; pair slot; stage
+  int group;                                          // (k, chunk) pairs per pipeline stage
   int debug;  // diagnostics (T2SC_CONV_DEBUG): 2 skips the MMAs, 4 the epilogue stores
   int *err;
+  long long *trace;  // diagnostics (T2SC_CONV_TRACE): per-stage clocks of CTA 0, or null
 };
+constexpr int kTraceN = 4096;
+#define T2SC_TRACE(slot, idx)                                                     \
+  do {                                                                            \
+    if (a.trace && blockIdx.x == 0 && (idx) < kTraceN) a.trace[(slot) * kTraceN + (idx)] = clock64(); \
+  } while (0)
 
 template <int DT>
 __device__ __forceinline__ uint32_t pack2(float a, float b) {
@@ -163,7 +178,7 @@ __device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, volatil
 }
 
 template <int DT, int RB>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(Roles<DT>::kThreads, 1)
     conv_tc_kernel(const TcArgs a) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // 1024-byte alignment for the swizzle atoms
@@ -172,15 +187,16 @@ __global__ void __launch_bounds__(kThreads, 1)
   // neighbour indices of a tile's active offsets, double-buffered across tiles
   int32_t *idx_buf = reinterpret_cast<int32_t *>(smem + (size_t)S * a.stage_bytes);
   uint64_t *bars = reinterpret_cast<uint64_t *>(idx_buf + 2 * kMaxK * kTileRows);
-  // bars: full[S], empty[S], tfull[2], tempty[2], mma_done, idx_full[2]
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * S + 7);
+  // bars: full[S], empty[S], tfull[2], tempty[2], mma_done, idx_full[2], idx_empty[2]
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * S + 9);
   volatile int *abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
   const uint32_t sbase = sm100::smem_u32(smem);
   const uint32_t full0 = sm100::smem_u32(bars), empty0 = full0 + 8 * S;
   const uint32_t tfull0 = empty0 + 8 * S, tempty0 = tfull0 + 16, mma_done = tempty0 + 16;
-  const uint32_t idxf0 = mma_done + 8;
+  const uint32_t idxf0 = mma_done + 8, idxe0 = idxf0 + 16;
 
   constexpr bool kSplit = DT == kModeTf32x3;
+  constexpr int kW = Roles<DT>::kCopyWarps, kControlWarp = Roles<DT>::kControlWarp, kMmaWarp = Roles<DT>::kMmaWarp;
   constexpr int ES = kSplit ? 4 : 2;   // element bytes
   constexpr int BKE = RB / ES;         // elements per chunk row
   const uint32_t a_tile = kTileRows * RB, b_tile = (uint32_t)a.bn * RB;
@@ -188,8 +204,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   if (tid == 0) {
     for (int s = 0; s < S; s++) {
-      // one cp.async completion arrival per producer thread + the weight copy's expect_tx
-      sm100::mbar_init(full0 + 8 * s, kProducerThreads + 1);
+      // one cp.async completion arrival per copy lane + the control warp's expect_tx
+      sm100::mbar_init(full0 + 8 * s, 32 * kW + 1);
       sm100::mbar_init(empty0 + 8 * s, 1);  // one tcgen05.commit
     }
     for (int b = 0; b < 2; b++) {
@@ -197,8 +213,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       sm100::mbar_init(tempty0 + 8 * b, kEpilogueThreads / 32);  // one arrival per epilogue warp
     }
     sm100::mbar_init(mma_done, 1);
-    sm100::mbar_init(idxf0, 1);
-    sm100::mbar_init(idxf0 + 8, 1);
+    for (int b = 0; b < 2; b++) {
+      sm100::mbar_init(idxf0 + 8 * b, 1);  // control warp's expect_tx
+      sm100::mbar_init(idxe0 + 8 * b, kW);  // every copy warp is done with the block
+    }
     *abort = 0;
     sm100::fence_mbar_init();
   }
@@ -212,98 +230,168 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem = *tmem_slot;
   const int nunits = a.ntiles * a.nco_tiles;
 
-  if (warp >= kProducerWarp0 && warp < kMmaWarp) {
-    // --------------------------- gather producers ---------------------------
-    // Lane (rsub, j) of producer warp w copies 16-byte vector j of tile rows
-    // 32w + p*RPP + rsub (p < CPR); its swizzled smem offsets are fixed.
-    constexpr int CPR = RB / 16;   // 16-byte vectors per row
-    constexpr int RPP = 32 / CPR;  // rows per warp pass
-    constexpr int EPV = 16 / ES;   // elements per vector
-    const int pw = warp - kProducerWarp0, ptid = tid - 32 * kProducerWarp0;
+  // tile masks are read ahead so no global-load latency sits at a unit boundary
+  auto mask_of = [&](int unit) -> uint32_t { return unit < nunits ? __ldg(a.tile_mask + unit / a.nco_tiles) : 0u; };
+  if (warp >= kCopyWarp0 && warp < kControlWarp) {
+    // ----------------------------- copy warps -----------------------------
+    // All copy warps fill every stage together: warp w owns tile rows
+    // [w*RW, (w+1)*RW). Lane (rsub, j) copies 16-byte vector j of rows
+    // w*RW + rsub*RPL + p (p < RPL): its RPL source indices are contiguous
+    // in the shared index block and each warp instruction moves 32/CPR
+    // whole rows. Each lane publishes its copies with
+    // cp.async.mbarrier.arrive.noinc, so up to S stages are in flight.
+    constexpr int CPR = RB / 16;          // 16-byte vectors per row
+    constexpr int RW = kTileRows / kW;    // rows per warp
+    constexpr int RPL = RW * CPR / 32;    // rows per lane
+    constexpr int EPV = 16 / ES;          // elements per vector
+    const int cw = warp - kCopyWarp0;
     const int j = lane % CPR, rsub = lane / CPR;
-    uint32_t soff[CPR];
+    const int row0 = cw * RW + rsub * RPL;
+    uint32_t soff[RPL];
 #pragma unroll
-    for (int p = 0; p < CPR; p++) soff[p] = swizzle_off((32 * pw + p * RPP + rsub) * RB + j * 16, RB);
-    const int64_t row_stride = (int64_t)a.ci * ES;
+    for (int p = 0; p < RPL; p++) soff[p] = swizzle_off((row0 + p) * RB + j * 16, RB);
+    const uint32_t row_stride = (uint32_t)(a.ci * ES);
     const int64_t lo_delta = kSplit ? (a.x_lo - a.x) : 0;
-    uint32_t it = 0, s = 0, ph = 0;  // stage iteration, its slot and phase
+    const int G = a.group;
+    uint32_t s = 0, ph = 0, t = 0;
     bool ok = true;
-    // thread 0 bulk-copies the [active k][128] neighbour-index block of a unit
-    auto load_idx = [&](int unit, int buf) {
-      const int tl = unit / a.nco_tiles;
-      uint32_t m = __ldg(a.tile_mask + tl);
-      const uint32_t bar = idxf0 + 8 * buf;
-      sm100::mbar_arrive_expect_tx(bar, (uint32_t)__popc(m) * kTileRows * 4);
-      const uint32_t dst = sm100::smem_u32(idx_buf + buf * kMaxK * kTileRows);
-      for (int slot = 0; m; slot++) {
-        const int k = __ffs(m) - 1;
-        m &= m - 1;
-        sm100::bulk_g2s(dst + slot * kTileRows * 4, a.nbr_sorted + (int64_t)k * a.n_pad + (int64_t)tl * kTileRows,
-                        kTileRows * 4, bar);
-      }
-    };
-    uint32_t n_idx_issued = 0;  // blocks requested (block i -> buffer i & 1)
-    uint32_t t = 0;             // blocks consumed
-    if (ptid == 0) load_idx(blockIdx.x, 0);
-    n_idx_issued++;
+    uint32_t km_next = mask_of(blockIdx.x);
     for (int u = blockIdx.x; u < nunits && ok; u += gridDim.x, t++) {
-      const int tile = u / a.nco_tiles, cot = u % a.nco_tiles;
-      // every producer thread is done reading the buffer the next prefetch overwrites
-      asm volatile("bar.sync 1, %0;" ::"n"(kProducerThreads) : "memory");
-      if (u + (int)gridDim.x < nunits) {
-        if (ptid == 0) load_idx(u + gridDim.x, n_idx_issued & 1);
-        n_idx_issued++;
-      }
-      if (!warp_wait(idxf0 + 8 * (t & 1), (t >> 1) & 1, abort, a.err)) {
+      uint32_t km = km_next;
+      km_next = mask_of(u + gridDim.x);
+      const int npairs = __popc(km) * a.nchunks;
+      if (npairs > 0 && !warp_wait(idxf0 + 8 * (t & 1), (t >> 1) & 1, abort, a.err)) {
         ok = false;
         break;
       }
-      const int32_t *idx_t = idx_buf + (t & 1) * kMaxK * kTileRows + 32 * pw + lane;
-      uint32_t km = __ldg(a.tile_mask + tile);
-      for (int slot = 0; km && ok; slot++) {
-        const int k = __ffs(km) - 1;
-        km &= km - 1;
-        const int32_t mysrc = idx_t[slot * kTileRows];
-        const uint8_t *gp[CPR];
-        uint32_t gs[CPR];
-#pragma unroll
-        for (int p = 0; p < CPR; p++) {
-          const int32_t src = __shfl_sync(0xffffffffu, mysrc, p * RPP + rsub);
-          gp[p] = a.x + (src >= 0 ? (int64_t)src * row_stride : 0) + j * 16;
-          gs[p] = src >= 0 ? 16u : 0u;
+      const int32_t *idx_t = idx_buf + (t & 1) * kMaxK * kTileRows + row0;
+      int c = a.nchunks, slot = -1;
+      const uint8_t *gp[RPL];
+      uint32_t gs[RPL];
+      for (int q = 0; q < npairs && ok;) {
+        if (!warp_wait(empty0 + 8 * s, ph ^ 1, abort, a.err)) {
+          ok = false;
+          break;
         }
-        const uint8_t *wsrc = a.wimg + (size_t)((size_t)cot * a.kvol + k) * a.nchunks * a.b_bytes;
-        for (int c = 0; c < a.nchunks; c++) {
-          if (!warp_wait(empty0 + 8 * s, ph ^ 1, abort, a.err)) {
-            ok = false;
-            break;
+        const uint32_t abase = sbase + s * a.stage_bytes, bar = full0 + 8 * s;
+        const int valid = npairs - q < G ? npairs - q : G;
+        for (int g = 0; g < valid; g++, q++) {
+          if (++c >= a.nchunks) {  // next active offset: its source rows
+            c = 0;
+            slot++;
+            const int32_t *ip = idx_t + slot * kTileRows;
+            int32_t src[RPL];
+            if (RPL >= 4) {
+#pragma unroll
+              for (int v = 0; v < RPL / 4; v++) {
+                const int4 q4 = reinterpret_cast<const int4 *>(ip)[v];
+                src[4 * v] = q4.x, src[4 * v + 1] = q4.y, src[4 * v + 2] = q4.z, src[4 * v + 3] = q4.w;
+              }
+            } else if (RPL == 2) {
+              const int2 q2 = *reinterpret_cast<const int2 *>(ip);
+              src[0] = q2.x, src[RPL - 1] = q2.y;
+            } else {
+              src[0] = ip[0];
+            }
+#pragma unroll
+            for (int p = 0; p < RPL; p++) {
+              gp[p] = a.x + (size_t)(src[p] >= 0 ? src[p] : 0) * row_stride + j * 16;
+              gs[p] = src[p] >= 0 ? 16u : 0u;
+            }
           }
-          const uint32_t abase = sbase + s * a.stage_bytes, bar = full0 + 8 * s;
-          if (ptid == 0) {
-            sm100::mbar_arrive_expect_tx(bar, a.b_bytes);
-            sm100::bulk_g2s(abase + a.a_bytes, wsrc + (size_t)c * a.b_bytes, a.b_bytes, bar);
-          }
+          const uint32_t sub = abase + g * a.sub_bytes;
           const bool cvalid = c * BKE + j * EPV < a.ci;
 #pragma unroll
-          for (int p = 0; p < CPR; p++) {
+          for (int p = 0; p < RPL; p++) {
             const uint32_t sz = cvalid ? gs[p] : 0u;
-            sm100::cp_async_16(abase + soff[p], gp[p] + c * RB, sz);
-            if (kSplit) sm100::cp_async_16(abase + a_tile + soff[p], gp[p] + lo_delta + c * RB, sz);
+            if (!(a.debug & 1)) {
+              sm100::cp_async_16(sub + soff[p], gp[p] + c * RB, sz);
+              if (kSplit) sm100::cp_async_16(sub + a_tile + soff[p], gp[p] + lo_delta + c * RB, sz);
+            }
           }
-          // arrives on the stage barrier once this thread's copies have landed
-          sm100::cp_async_arrive_noinc(bar);
-          it++;
-          if (++s == (uint32_t)S) {
-            s = 0;
-            ph ^= 1;
+        }
+        // arrives on the stage barrier once this lane's copies have landed
+        sm100::cp_async_arrive_noinc(bar);
+        if (++s == (uint32_t)S) {
+          s = 0;
+          ph ^= 1;
+        }
+      }
+      __syncwarp();
+      if (lane == 0) sm100::mbar_arrive(idxe0 + 8 * (t & 1));
+    }
+    sm100::cp_async_wait<0>();
+  } else if (warp == kControlWarp) {
+    // ---------------------------- control warp ----------------------------
+    // Per unit: prefetch the next unit's neighbour-index block (lane i
+    // copies the block of the i-th active offset), then issue the weight
+    // block of every stage iteration of this unit.
+    auto load_idx = [&](int unit, int buf, uint32_t m) {
+      const int tl = unit / a.nco_tiles;
+      const uint32_t bar = idxf0 + 8 * buf;
+      const int nk = __popc(m);
+      if (lane == 0) sm100::mbar_arrive_expect_tx(bar, (uint32_t)nk * kTileRows * 4);
+      __syncwarp();
+      if (lane < nk) {
+        const int k = __fns(m, 0, lane + 1);
+        const uint32_t dst = sm100::smem_u32(idx_buf + buf * kMaxK * kTileRows) + lane * kTileRows * 4;
+        sm100::bulk_g2s(dst, a.nbr_sorted + (int64_t)k * a.n_pad + (int64_t)tl * kTileRows, kTileRows * 4, bar);
+      }
+    };
+    uint32_t it = 0, s = 0, ph = 0, t = 0, n_idx = 0;
+    bool ok = true;
+    uint32_t km_cur = mask_of(blockIdx.x), km_n1 = mask_of(blockIdx.x + gridDim.x);
+    load_idx(blockIdx.x, 0, km_cur);  // buffer 0 starts free
+    n_idx = 1;
+    for (int u = blockIdx.x; u < nunits && ok; u += gridDim.x, t++) {
+      const int cot = u % a.nco_tiles;
+      const uint32_t km = km_cur;
+      const uint32_t km_n2 = mask_of(u + 2 * gridDim.x);
+      if (u + (int)gridDim.x < nunits) {
+        // the other buffer held unit t-1: wait until every copy warp is done with it
+        const uint32_t nb = (t + 1) & 1;
+        if (!warp_wait(idxe0 + 8 * nb, (((t + 1) >> 1) & 1) ^ 1, abort, a.err)) {
+          ok = false;
+          break;
+        }
+        load_idx(u + gridDim.x, nb, km_n1);
+        n_idx++;
+      }
+      km_cur = km_n1;
+      km_n1 = km_n2;
+      // weight blocks: G (k, chunk) pairs per stage, in the copy warps' order
+      const int npairs = __popc(km) * a.nchunks;
+      uint32_t m = km;
+      int c = a.nchunks;
+      const uint8_t *wk = a.wimg;
+      for (int q = 0; q < npairs && ok;) {
+        if (!warp_wait(empty0 + 8 * s, ph ^ 1, abort, a.err)) {
+          ok = false;
+          break;
+        }
+        const int valid = npairs - q < a.group ? npairs - q : a.group;
+        const uint32_t bar = full0 + 8 * s, abase = sbase + s * a.stage_bytes;
+        if (lane == 0) sm100::mbar_arrive_expect_tx(bar, (uint32_t)valid * a.b_bytes);
+        for (int g = 0; g < valid; g++, q++) {
+          if (++c >= a.nchunks) {
+            c = 0;
+            const int k = __ffs(m) - 1;
+            m &= m - 1;
+            wk = a.wimg + (size_t)((size_t)cot * a.kvol + k) * a.nchunks * a.b_bytes;
           }
+          if (lane == 0)
+            sm100::bulk_g2s(abase + g * a.sub_bytes + a.a_bytes, wk + (size_t)c * a.b_bytes, a.b_bytes, bar);
+        }
+        it++;
+        if (++s == (uint32_t)S) {
+          s = 0;
+          ph ^= 1;
         }
       }
     }
-    sm100::cp_async_wait<0>();
-    if (ptid == 0) {
+    if (lane == 0) {
       // copies requested but never consumed (abort path) land before exit
-      for (uint32_t i2 = t; i2 < n_idx_issued && (int)(blockIdx.x + i2 * gridDim.x) < nunits; i2++)
+      for (uint32_t i2 = t; i2 < n_idx; i2++)
         sm100::mbar_wait_cycles(idxf0 + 8 * (i2 & 1), (i2 >> 1) & 1, kWaitLimit / 8);
       if (!ok) {
         const uint32_t first = it > (uint32_t)S ? it - S : 0;
@@ -317,10 +405,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int row = 32 * q + lane;
     uint32_t acc_it = 0;
     float part[kSplit ? kTf32MaxBn : 1];
+    // the next unit's mask and output row are read one unit ahead
+    auto orow_of = [&](int unit) -> int {
+      return unit < nunits ? __ldg(a.perm + (int64_t)(unit / a.nco_tiles) * kTileRows + row) : -1;
+    };
+    uint32_t km_next = mask_of(blockIdx.x);
+    int orow_next = orow_of(blockIdx.x);
     for (int u = blockIdx.x; u < nunits; u += gridDim.x) {
-      const int tile = u / a.nco_tiles, cot = u % a.nco_tiles;
-      const uint32_t km = __ldg(a.tile_mask + tile);
-      const int orow = __ldg(a.perm + (int64_t)tile * kTileRows + row);
+      const int cot = u % a.nco_tiles;
+      const uint32_t km = km_next;
+      const int orow = orow_next;
+      km_next = mask_of(u + gridDim.x);
+      orow_next = orow_of(u + gridDim.x);
       const int col0 = cot * a.bn;
       if (km == 0) {
         if (orow >= 0) {
@@ -374,7 +470,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         continue;
       }
       const uint32_t b = acc_it & 1;
+      if (tid == 0) T2SC_TRACE(4, acc_it);
       if (!warp_wait(tfull0 + 8 * b, (acc_it >> 1) & 1, abort, a.err)) break;
+      if (tid == 0) T2SC_TRACE(5, acc_it);
       sm100::tc_fence_after();
       const uint32_t tbase = tmem + ((uint32_t)(32 * q) << 16) + b * a.bn;
       for (int cc = 0; cc < a.bn; cc += 16) {
@@ -399,16 +497,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       // descriptors of stage 0; a stage or k-step offset is added to the
       // 14-bit start-address field (all of shared memory fits in it)
       const uint64_t dA = sm100::smem_desc(sbase, RB), dB = sm100::smem_desc(sbase + a.a_bytes, RB);
-      uint32_t s = 0, ph = 0, acc_it = 0;
+      uint32_t s = 0, ph = 0, acc_it = 0, mit = 0;
       bool ok = true;
+      uint32_t km_next = mask_of(blockIdx.x);
       for (int u = blockIdx.x; u < nunits && ok; u += gridDim.x) {
-        const int tile = u / a.nco_tiles;
-        const uint32_t km = __ldg(a.tile_mask + tile);
+        const uint32_t km = km_next;
+        km_next = mask_of(u + gridDim.x);
         if (km == 0) continue;
         const int nk = __popc(km);
-        // split-TF32: one accumulator (and one drain) per offset; otherwise one per tile
-        const int groups = kSplit ? nk : 1, steps_per_group = kSplit ? a.nchunks : nk * a.nchunks;
-        for (int g = 0; g < groups && ok; g++) {
+        // split-TF32: one accumulator (and one drain) per offset (G = 1);
+        // otherwise one per unit. A stage holds up to G (k, chunk) pairs.
+        const int groups = kSplit ? nk : 1, pairs_per_group = kSplit ? a.nchunks : nk * a.nchunks;
+        for (int gi = 0; gi < groups && ok; gi++) {
           const uint32_t b = acc_it & 1;
           if (!sm100::mbar_wait_bounded(tempty0 + 8 * b, ((acc_it >> 1) & 1) ^ 1, abort, a.err, kDevErrTimeout,
                                         kWaitLimit)) {
@@ -418,28 +518,34 @@ __global__ void __launch_bounds__(kThreads, 1)
           sm100::tc_fence_after();
           const uint32_t dtm = tmem + b * a.bn;
           uint32_t accum = 0;
-          for (int st = 0; st < steps_per_group; st++) {
+          for (int q = 0; q < pairs_per_group; q += a.group) {
+            T2SC_TRACE(2, mit);
             if (!sm100::mbar_wait_bounded(full0 + 8 * s, ph, abort, a.err, kDevErrTimeout, kWaitLimit)) {
               ok = false;
               break;
             }
             sm100::tc_fence_after();
-            const uint64_t so = (s * a.stage_bytes) >> 4;
+            const int valid = pairs_per_group - q < a.group ? pairs_per_group - q : a.group;
+            for (int g = 0; g < valid; g++) {
+              const uint64_t so = (s * a.stage_bytes + g * a.sub_bytes) >> 4;
 #pragma unroll
-            for (int kk = 0; kk < RB / 32; kk++) {
-              const uint64_t ahi = dA + so + kk * 2, bhi = dB + so + kk * 2;
-              if (a.debug & 2) {
-              } else if (kSplit) {
-                const uint64_t alo = ahi + (a_tile >> 4), blo = bhi + (b_tile >> 4);
-                sm100::mma_tf32(dtm, alo, bhi, idesc, accum);
-                sm100::mma_tf32(dtm, ahi, blo, idesc, 1u);
-                sm100::mma_tf32(dtm, ahi, bhi, idesc, 1u);
-              } else {
-                sm100::mma_f16(dtm, ahi, bhi, idesc, accum);
+              for (int kk = 0; kk < RB / 32; kk++) {
+                const uint64_t ahi = dA + so + kk * 2, bhi = dB + so + kk * 2;
+                if (a.debug & 2) {
+                } else if (kSplit) {
+                  const uint64_t alo = ahi + (a_tile >> 4), blo = bhi + (b_tile >> 4);
+                  sm100::mma_tf32(dtm, alo, bhi, idesc, accum);
+                  sm100::mma_tf32(dtm, ahi, blo, idesc, 1u);
+                  sm100::mma_tf32(dtm, ahi, bhi, idesc, 1u);
+                } else {
+                  sm100::mma_f16(dtm, ahi, bhi, idesc, accum);
+                }
+                accum = 1;
               }
-              accum = 1;
             }
             sm100::mma_commit(empty0 + 8 * s);
+            T2SC_TRACE(3, mit);
+            mit++;
             if (++s == (uint32_t)S) {
               s = 0;
               ph ^= 1;
@@ -486,7 +592,25 @@ template <int DT, int RB>
 int launch_tc(t2sc_conv *cv, const TcArgs &args, int grid, size_t smem, std::string &err) {
   auto kfn = conv_tc_kernel<DT, RB>;
   T2SC_CUDA(cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem), "tc smem attr");
-  kfn<<<grid, kThreads, smem, cv->ctx->stream>>>(args);
+  const char *trace_path = getenv("T2SC_CONV_TRACE");
+  if (trace_path) {  // diagnostics only: allocates, synchronises and writes a file
+    TcArgs t = args;
+    const size_t bytes = 10 * kTraceN * sizeof(long long);
+    T2SC_CUDA(cudaMalloc((void **)&t.trace, bytes), "trace");
+    T2SC_CUDA(cudaMemset(t.trace, 0, bytes), "trace");
+    kfn<<<grid, Roles<DT>::kThreads, smem, cv->ctx->stream>>>(t);
+    T2SC_LAUNCHED(cv->ctx, "conv_tc");
+    std::vector<long long> h(10 * kTraceN);
+    T2SC_CUDA(cudaMemcpyAsync(h.data(), t.trace, bytes, cudaMemcpyDeviceToHost, cv->ctx->stream), "trace");
+    T2SC_CUDA(cudaStreamSynchronize(cv->ctx->stream), "trace");
+    cudaFree(t.trace);
+    if (FILE *f = fopen(trace_path, "wb")) {
+      fwrite(h.data(), 1, bytes, f);
+      fclose(f);
+    }
+    return T2SC_OK;
+  }
+  kfn<<<grid, Roles<DT>::kThreads, smem, cv->ctx->stream>>>(args);
   T2SC_LAUNCHED(cv->ctx, "conv_tc");
   return T2SC_OK;
 }
@@ -588,15 +712,25 @@ int conv_tc_launch(t2sc_conv *cv, t2sc_map *m, const void *x, void *y, int flags
     return e ? atoi(e) : 0;
   }();
   a.debug = debug_bits;
+  a.trace = nullptr;
   int cols = 32;
   while (cols < 2 * cv->bn) cols <<= 1;
   a.tmem_cols = cols;
   const int na = cv->dtype == T2SC_DT_F32 ? 2 : 1;
   a.a_bytes = kTileRows * cv->row_bytes * na;
   a.b_bytes = (uint32_t)cv->bn * cv->row_bytes * na;
-  a.stage_bytes = (a.a_bytes + a.b_bytes + 1023u) & ~1023u;
+  a.sub_bytes = (a.a_bytes + a.b_bytes + 1023u) & ~1023u;
   const int idx_bytes = 2 * kMaxK * kTileRows * 4;  // double-buffered tile index blocks
-  int S = (kSmemMax - idx_bytes - 1280) / (int)a.stage_bytes;
+  const int avail = kSmemMax - idx_bytes - 1280;
+  // Small pairs are grouped so that one stage carries up to ~48 KB: the
+  // per-stage handshake is then paid once per several MMA k-steps.
+  // Split-TF32 drains per offset, so it keeps one pair per stage.
+  int G = 1;
+  if (cv->dtype != T2SC_DT_F32)
+    while (G < 4 && (int)((G + 1) * a.sub_bytes) <= 48 * 1024 && avail / (int)((G + 1) * a.sub_bytes) >= 4) G++;
+  a.group = G;
+  a.stage_bytes = G * a.sub_bytes;
+  int S = avail / (int)a.stage_bytes;
   if (S > 8) S = 8;
   if (S < kMinStages) {
     err = "conv tile does not fit shared memory";
