@@ -149,6 +149,24 @@ int t2sc_subdivide_device(t2sc_ctx *ctx, const int32_t *coords, int64_t n, const
                           int32_t *out_coords, void *out_feats, int32_t *out_parent,
                           int32_t *out_subidx, int64_t *m);
 
+/* Allocation-free variant of t2sc_subdivide_device. It has no counterpart in
+ * the reference; it exists for callers that may not allocate device memory
+ * while they run (a runtime that hands the library a fixed memory budget up
+ * front, or an engine that keeps the CUDA allocator and its implicit
+ * synchronisation out of a decode pass). Its scratch (keep masks, counts,
+ * offsets, scan block sums: about 13.6 MB) is one static device array per
+ * GPU that loads the library, held until the process exits, sized for at
+ * most 1,048,576 parents: a larger n is rejected with T2SC_ERR_INVALID and
+ * a message. out_parent and out_subidx are required (int32 [8N] each).
+ * The first call on a device looks up the array's device address; make
+ * that first call before any stream capture. Every call on a device shares
+ * the array, so calls that overlap on the GPU (other streams or contexts)
+ * race; serialise them. Results are identical to t2sc_subdivide_device. */
+int t2sc_subdivide_noalloc_device(t2sc_ctx *ctx, const int32_t *coords, int64_t n, const float *sub,
+                                  int keep_mode, const void *feats, int c, int feats_mode, int dtype,
+                                  int32_t *out_coords, void *out_feats, int32_t *out_parent,
+                                  int32_t *out_subidx, int64_t *m);
+
 /* ---- synthetic inputs (seeded shells of the benchmark configurations) ----
  * Active cells of a G^3 grid with | |p-c| - R(1 + 0.1 sin(3t) cos(2(f+phase))) | <= h,
  * c = G/2, t = acos((p_z-c)/|p-c|), f = atan2(p_y-c, p_x-c), phase = 0 for

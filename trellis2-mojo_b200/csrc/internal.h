@@ -95,6 +95,12 @@ int export_csr(t2sc_coords *c, t2sc_map *m, int64_t *row_start, int64_t *src_s, 
 // out[i] = sum(in[0..i)), *total (device int64) = sum(in). Scratch is
 // allocated stream-ordered on `stream` and released before return.
 int scan_counts(t2sc_ctx *ctx, const int32_t *in, int64_t n, int64_t *out, int64_t *d_total);
+// Same scan with caller-provided block-sum scratch of scan_block_count(n)
+// int64 entries; allocates nothing.
+constexpr int64_t kScanTileItems = 2048;  // items per scan block (256 threads x 8)
+inline int64_t scan_block_count(int64_t n) { return (n + kScanTileItems - 1) / kScanTileItems; }
+int scan_counts_into(t2sc_ctx *ctx, const int32_t *in, int64_t n, int64_t *out, int64_t *d_total,
+                     int64_t *block_sums);
 
 // ---- conv kernels ----
 int conv_tc_prepare(t2sc_conv *cv, const float *w_host, std::string &err);

@@ -79,4 +79,22 @@ int scan_counts(t2sc_ctx *ctx, const int32_t *in, int64_t n, int64_t *out, int64
   return T2SC_OK;
 }
 
+int scan_counts_into(t2sc_ctx *ctx, const int32_t *in, int64_t n, int64_t *out, int64_t *d_total,
+                     int64_t *block_sums) {
+  static_assert(kScanTile == kScanTileItems, "scan tile size");
+  std::string &err = ctx->last_error;
+  if (n <= 0) {
+    if (d_total) T2SC_CUDA(cudaMemsetAsync(d_total, 0, sizeof(int64_t), ctx->stream), "scan memset");
+    return T2SC_OK;
+  }
+  const int64_t nb = scan_block_count(n);
+  scan_reduce_kernel<<<(unsigned)nb, kScanThreads, 0, ctx->stream>>>(in, n, block_sums);
+  T2SC_LAUNCHED(ctx, "scan_reduce");
+  scan_blocks_kernel<<<1, 1024, 0, ctx->stream>>>(block_sums, nb, d_total);
+  T2SC_LAUNCHED(ctx, "scan_blocks");
+  scan_apply_kernel<<<(unsigned)nb, kScanThreads, 0, ctx->stream>>>(in, n, block_sums, out);
+  T2SC_LAUNCHED(ctx, "scan_apply");
+  return T2SC_OK;
+}
+
 }  // namespace t2sc

@@ -10,6 +10,8 @@
 // (2) an exclusive shuffle-scan of the counts (scan.cu) gives each parent's
 // first output row; (3) children and their feature rows are written, the
 // features as 16-byte vectors when the row size allows.
+#include <mutex>
+
 #include "internal.h"
 
 namespace t2sc {
@@ -115,3 +117,143 @@ int subdivide_device(t2sc_ctx *ctx, const int32_t *coords, int64_t n, const floa
 }
 
 }  // namespace t2sc
+
+// ---------------------------------------------------------------------------
+// Allocation-free subdivision (t2sc_subdivide_noalloc_device).
+//
+// Some callers cannot allocate device memory while they run this step: a
+// host runtime that hands the library a fixed memory budget up front, or an
+// engine that must not touch the CUDA allocator (and its implicit
+// synchronisation) in the middle of a decode pass. For them the scratch of
+// the subdivision (keep masks, per-parent counts and offsets, and the scan's
+// block sums) lives in one file-scope device array instead of stream-ordered
+// allocations. Its size is fixed at build time for up to
+// kNoAllocMaxParents parents; every GPU that loads the library holds it
+// until the process exits.
+namespace t2sc {
+namespace {
+
+constexpr int64_t kNoAllocMaxParents = int64_t(1) << 20;
+constexpr size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
+constexpr size_t kNaMasks = 0;
+constexpr size_t kNaCounts = align256(kNaMasks + kNoAllocMaxParents);
+constexpr size_t kNaOffs = align256(kNaCounts + 4 * kNoAllocMaxParents);
+constexpr size_t kNaBlocks = align256(kNaOffs + 8 * (kNoAllocMaxParents + 1));
+constexpr size_t kNaBytes =
+    align256(kNaBlocks + 8 * ((kNoAllocMaxParents + kScanTileItems - 1) / kScanTileItems));
+
+// Shared by every call on a device; the last call's contents stay in it.
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNaBytes];
+
+// Device address of g_noalloc_scratch per device, looked up once with that
+// device current (in host code the symbol is only a host-side handle).
+std::mutex g_noalloc_mu;
+uint8_t *g_noalloc_ptr[128] = {};
+
+int noalloc_scratch(int device, uint8_t **out, std::string &err) {
+  if (device < 0 || device >= 128) {
+    err = "device ordinal out of range";
+    return T2SC_ERR_INVALID;
+  }
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_ptr[device]) {
+    void *p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess) {
+      err = std::string("cudaGetSymbolAddress(no-alloc scratch): ") + cudaGetErrorString(e);
+      return T2SC_ERR_CUDA;
+    }
+    g_noalloc_ptr[device] = static_cast<uint8_t *>(p);
+  }
+  *out = g_noalloc_ptr[device];
+  return T2SC_OK;
+}
+
+}  // namespace
+}  // namespace t2sc
+
+extern "C" int t2sc_subdivide_noalloc_device(t2sc_ctx *ctx, const int32_t *coords, int64_t n, const float *sub,
+                                             int keep_mode, const void *feats, int c, int feats_mode, int dtype,
+                                             int32_t *out_coords, void *out_feats, int32_t *out_parent,
+                                             int32_t *out_subidx, int64_t *m) {
+  using namespace t2sc;
+  if (!ctx) return T2SC_ERR_INVALID;
+  std::string &err = ctx->last_error;
+  if (!m) {
+    err = "subdivide_noalloc: null m";
+    return T2SC_ERR_INVALID;
+  }
+  *m = 0;
+  if (n < 0 || n > kNoAllocMaxParents) {
+    err = "subdivide_noalloc: n = " + std::to_string(n) + " parents is outside the static scratch limit of " +
+          std::to_string(kNoAllocMaxParents) + "; use t2sc_subdivide_device";
+    return T2SC_ERR_INVALID;
+  }
+  if (keep_mode != T2SC_SUB_NONZERO && keep_mode != T2SC_SUB_POSITIVE) {
+    err = "subdivide_noalloc: unknown keep mode";
+    return T2SC_ERR_INVALID;
+  }
+  if (feats_mode != T2SC_FEATS_NONE && feats_mode != T2SC_FEATS_UPSAMPLE && feats_mode != T2SC_FEATS_C2S) {
+    err = "subdivide_noalloc: unknown feature mode";
+    return T2SC_ERR_INVALID;
+  }
+  if (dtype != T2SC_DT_F32 && dtype != T2SC_DT_F16 && dtype != T2SC_DT_BF16) {
+    err = "subdivide_noalloc: unknown dtype";
+    return T2SC_ERR_INVALID;
+  }
+  if (n == 0) return T2SC_OK;
+  if (!coords || !sub || !out_coords || !out_parent || !out_subidx ||
+      (feats_mode != T2SC_FEATS_NONE && (!feats || !out_feats || c <= 0))) {
+    err = "subdivide_noalloc: null buffer (out_parent and out_subidx are required here)";
+    return T2SC_ERR_INVALID;
+  }
+  int prev = -1;
+  if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+  if (prev != ctx->device) cudaSetDevice(ctx->device);
+  int rc = [&]() -> int {
+    uint8_t *scr = nullptr;
+    int r = noalloc_scratch(ctx->device, &scr, err);
+    if (r != T2SC_OK) return r;
+    uint8_t *masks = scr + kNaMasks;
+    int32_t *counts = reinterpret_cast<int32_t *>(scr + kNaCounts);
+    int64_t *offs = reinterpret_cast<int64_t *>(scr + kNaOffs);
+    int64_t *blocks = reinterpret_cast<int64_t *>(scr + kNaBlocks);
+    cudaStream_t st = ctx->stream;
+    // every scratch word read below is first written by this call (masks and
+    // counts for all n parents, offsets and block sums by the scan), so
+    // nothing has to be cleared
+    sub_count_kernel<<<nblk(n), 256, 0, st>>>(sub, n, keep_mode == T2SC_SUB_POSITIVE, masks, counts);
+    T2SC_LAUNCHED(ctx, "sub_count");
+    r = scan_counts_into(ctx, counts, n, offs, offs + n, blocks);
+    if (r != T2SC_OK) return r;
+    sub_emit_kernel<<<nblk(n), 256, 0, st>>>((const int4 *)coords, masks, offs, n, (int4 *)out_coords, out_parent,
+                                            out_subidx);
+    T2SC_LAUNCHED(ctx, "sub_emit");
+    int64_t mm = 0;
+    T2SC_CUDA(cudaMemcpyAsync(&mm, offs + n, sizeof(int64_t), cudaMemcpyDeviceToHost, st), "subdivide count");
+    T2SC_CUDA(cudaStreamSynchronize(st), "subdivide count");
+    if (feats_mode != T2SC_FEATS_NONE && mm > 0) {
+      const int64_t row_bytes = (int64_t)c * (dtype == T2SC_DT_F32 ? 4 : 2);
+      const int c2s = feats_mode == T2SC_FEATS_C2S;
+      if (row_bytes % 16 == 0) {
+        const int vpr = (int)(row_bytes / 16);
+        sub_feats_kernel<uint4><<<nblk(mm * vpr), 256, 0, st>>>((const uint4 *)feats, (uint4 *)out_feats, out_parent,
+                                                               out_subidx, mm, vpr, c2s);
+      } else if (row_bytes % 4 == 0) {
+        const int vpr = (int)(row_bytes / 4);
+        sub_feats_kernel<uint32_t><<<nblk(mm * vpr), 256, 0, st>>>((const uint32_t *)feats, (uint32_t *)out_feats,
+                                                                  out_parent, out_subidx, mm, vpr, c2s);
+      } else {
+        const int vpr = (int)(row_bytes / 2);
+        sub_feats_kernel<uint16_t><<<nblk(mm * vpr), 256, 0, st>>>((const uint16_t *)feats, (uint16_t *)out_feats,
+                                                                  out_parent, out_subidx, mm, vpr, c2s);
+      }
+      T2SC_LAUNCHED(ctx, "sub_feats");
+    }
+    *m = mm;
+    return T2SC_OK;
+  }();
+  int cur = -1;
+  if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+  return rc;
+}

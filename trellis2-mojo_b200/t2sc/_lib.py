@@ -47,6 +47,7 @@ SIGNATURES = {
     "t2sc_conv_chain_forward": (I32, [P, I32, P, P, P, P]),
     "t2sc_subdivide": (I32, [P, P, I64, P, I32, P, I32, I32, P, P, P, P, PI64]),
     "t2sc_subdivide_device": (I32, [P, P, I64, P, I32, P, I32, I32, I32, P, P, P, P, PI64]),
+    "t2sc_subdivide_noalloc_device": (I32, [P, P, I64, P, I32, P, I32, I32, I32, P, P, P, P, PI64]),
     "t2sc_synth_shell": (I32, [I32, D, D, U64, I32, P, I64, PI64]),
     "t2sc_synth_normal": (I32, [U64, F, P, I64]),
     "t2sc_synth_bernoulli": (I32, [U64, D, P, I64]),
