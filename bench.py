@@ -186,7 +186,6 @@ def main():
     if args.impl == "reference":
         return run_reference(args)
     if args.gpus > 1 or int(os.environ.get("WORLD_SIZE", "1")) > 1:
-        from bench_dist import run_distributed
         return run_distributed(args)
     return run_single(args)
 
@@ -300,7 +299,7 @@ def run_single(args):
                "sample": f"layer 1, first {ne} of {etot} edges (kernel-offset-major), reference Co-chunk "
                          f"parallelism ({C // 8} threads), {dt:.1f} s"}
     line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": 1, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "mvoxel_per_s": mvox, "map_build_ms": map_ms,
             "config": {"workload": WORKLOAD, "voxels": n, "edges": E, "layers": LAYERS, "channels": C,
@@ -316,6 +315,125 @@ def run_single(args):
             "clocks": clk.summary,
             "cpu_baseline": cpu}
     print(json.dumps(line))
+
+
+def run_distributed(args):
+    """One rank per GPU (torchrun): the cfg4 shell is cut into z-slabs
+    (t2sc.dist); before every layer each rank receives its one-voxel halo
+    from its z-neighbours over NCCL, then convolves (own + halo) rows with
+    outputs for its own rows. Total work is fixed as N grows (strong
+    scaling); `value` is the whole job's TFLOP/s over the slowest rank."""
+    import torch
+    import torch.distributed as tdist
+
+    import t2sc
+    from t2sc import _lib, dist
+
+    rank, world = int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", str(rank)))
+    torch.cuda.set_device(local)
+    tdist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    ctx = t2sc.Context.default(local)
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
+    ctx.set_stream(stream.cuda_stream)
+    coords, x, ws, bs = inputs()
+    slab = dist.partition(coords, world)[rank]
+    rows = slab.rows
+    n_own, n_loc = slab.n_own, len(rows)
+    convs = [t2sc.SparseConv3d(w, b, dtype="bf16", ctx=ctx) for w, b in zip(ws, bs)]
+    cdev = t2sc.Coords(ctx, coords[rows], n_targets=n_own)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    e_loc = cdev.build_map()
+    torch.cuda.synchronize()
+    map_ms = 1e3 * (time.perf_counter() - t0)
+    e_all = torch.tensor([e_loc], dtype=torch.int64, device="cuda")
+    tdist.all_reduce(e_all)
+    E = int(e_all.item())
+
+    xin = torch.zeros((n_loc, C), dtype=torch.bfloat16, device="cuda")
+    xin[:n_own] = torch.from_numpy(x[slab.own]).to("cuda").to(torch.bfloat16)
+    bufs = [torch.zeros((n_loc, C), dtype=torch.bfloat16, device="cuda") for _ in range(2)]
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device="cuda")
+    L = _lib.lib
+
+    def step():
+        cur = xin
+        for i, cv in enumerate(convs):
+            dist.exchange_halo(cur, slab, tdist)  # halo rows of this layer's input
+            out = bufs[i & 1]
+            _lib.check(L.t2sc_conv_forward_device(cv.handle, cdev.handle, ctypes.c_void_p(cur.data_ptr()),
+                                                  ctypes.c_void_p(out.data_ptr()), _lib.SILU, None), ctx.handle)
+            cur = out
+        return cur
+
+    for _ in range(args.warmup):
+        step()
+    ctx.synchronize()
+    torch.cuda.synchronize()
+    ev = lambda: torch.cuda.Event(enable_timing=True)  # noqa: E731
+    times = []
+    launches0 = ctx.launch_count()
+    clk = Clocks(local).__enter__() if rank == 0 else None
+    time.sleep(0.3)
+    for _ in range(args.steps):
+        flush.zero_()
+        torch.cuda.synchronize()
+        tdist.barrier()
+        s0, s1 = ev(), ev()
+        s0.record(stream)
+        step()
+        s1.record(stream)
+        torch.cuda.synchronize()
+        times.append(s0.elapsed_time(s1))
+    launches = ctx.launch_count() - launches0
+    t_load = time.perf_counter()
+    while time.perf_counter() - t_load < 1.0:
+        for _ in range(10):
+            step()
+        torch.cuda.synchronize()
+    if clk:
+        clk.__exit__()
+    tt = torch.tensor(times, dtype=torch.float64, device="cuda")
+    tdist.all_reduce(tt, op=tdist.ReduceOp.MAX)  # per step, the slowest rank
+    ms = float(tt.sum().item()) / args.steps
+
+    # e2e: each rank uploads its own rows from pinned host f32, runs the
+    # chain with halo exchanges, downloads its own outputs as f32
+    xh = torch.from_numpy(np.ascontiguousarray(x[slab.own])).pin_memory()
+    yh = torch.empty((n_own, C), dtype=torch.float32).pin_memory()
+    e2e = []
+    for s in range(args.steps + 2):
+        torch.cuda.synchronize()
+        tdist.barrier()
+        t0 = time.perf_counter()
+        xin[:n_own].copy_(xh.to("cuda", non_blocking=True))
+        out = step()
+        yh.copy_(out[:n_own].float(), non_blocking=True)
+        torch.cuda.synchronize()
+        if s >= 2:
+            e2e.append(time.perf_counter() - t0)
+    et = torch.tensor(e2e, dtype=torch.float64, device="cuda")
+    tdist.all_reduce(et, op=tdist.ReduceOp.MAX)
+    e2e_s = float(et.sum().item()) / args.steps
+    if rank == 0:
+        flops = LAYERS * 2.0 * E * C * C
+        n = len(coords)
+        line = {"metric": METRIC, "value": flops / (ms * 1e-3) / 1e12, "unit": UNIT, "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+                "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+                "mvoxel_per_s": LAYERS * n / (ms * 1e-3) / 1e6, "map_build_ms": map_ms,
+                "config": {"workload": WORKLOAD, "voxels": n, "edges": E, "layers": LAYERS, "channels": C,
+                           "l2": "flushed between steps (256 MiB write)",
+                           "parallelism": f"z-slab x{world}, one-voxel halo over NCCL send/recv",
+                           "rank0_rows": n_own, "rank0_halo_rows": n_loc - n_own},
+                "e2e": {"value": flops / e2e_s / 1e12, "unit": UNIT, "h2d_bytes_per_step": n * C * 4,
+                        "d2h_bytes_per_step": n * C * 4, "ms_per_step": 1e3 * e2e_s},
+                "gpu_launches": launches, "clocks": clk.summary if clk else None, "cpu_baseline": None}
+        print(json.dumps(line))
+    tdist.barrier()
+    tdist.destroy_process_group()
 
 
 if __name__ == "__main__":

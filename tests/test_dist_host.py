@@ -1,0 +1,84 @@
+"""Host logic of the z-slab partition (CPU): neighbourhoods are complete
+on every rank, sends and receives line up, and the halo exchange moves the
+right rows between world-size-2 and -3 gloo ranks."""
+import os
+
+import numpy as np
+import pytest
+
+
+def _local_map_matches_global(oracle, coords, slabs):
+    src, tgt, kidx = oracle.neighbor_map(coords)
+    glob = {}
+    for s_, t_, k_ in zip(src, tgt, kidx):
+        glob.setdefault(int(t_), set()).add((int(s_), int(k_)))
+    for sl in slabs:
+        rows = sl.rows
+        ls, lt, lk = oracle.neighbor_map(coords[rows])
+        loc = {}
+        for s_, t_, k_ in zip(ls, lt, lk):
+            if t_ < sl.n_own:
+                loc.setdefault(int(rows[t_]), set()).add((int(rows[s_]), int(k_)))
+        for g in sl.own:
+            assert loc.get(int(g), set()) == glob.get(int(g), set())
+
+
+@pytest.mark.parametrize("world", [2, 3, 8])
+def test_partition_neighbourhoods_complete(t2sc, oracle, world):
+    from t2sc import dist
+    coords = t2sc.synth.shell(*t2sc.synth.SHELLS["cfg1"])
+    slabs = dist.partition(coords, world)
+    own = np.concatenate([s.own for s in slabs])
+    assert np.array_equal(np.sort(own), np.arange(len(coords)))
+    sizes = [s.n_own for s in slabs]
+    assert max(sizes) < 1.5 * len(coords) / world
+    for r, s in enumerate(slabs):
+        if r > 0:
+            assert np.array_equal(s.halo_lo, slabs[r - 1].own[slabs[r - 1].hi_send])
+        if r < world - 1:
+            assert np.array_equal(s.halo_hi, slabs[r + 1].own[slabs[r + 1].lo_send])
+    _local_map_matches_global(oracle, coords, slabs)
+
+
+def test_partition_rejects_too_thin(t2sc):
+    from t2sc import dist
+    with pytest.raises(ValueError):
+        dist.partition(t2sc.synth.blob(3), 2)
+
+
+def _worker(rank, world, port, q):
+    import sys
+    here = os.path.dirname(os.path.abspath(__file__))
+    sys.path[:0] = [os.path.dirname(here), os.path.join(os.path.dirname(here), "trellis2-mojo_b200")]
+    import torch
+    import torch.distributed as tdist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    tdist.init_process_group("gloo", rank=rank, world_size=world)
+    from t2sc import dist, synth
+    coords = synth.shell(*synth.SHELLS["cfg1"])
+    glob = torch.from_numpy(synth.normal(5, (len(coords), 6)))
+    sl = dist.partition(coords, world)[rank]
+    rows = torch.from_numpy(sl.rows)
+    local = torch.zeros((len(rows), 6))
+    local[:sl.n_own] = glob[rows[:sl.n_own]]
+    dist.exchange_halo(local, sl, tdist)
+    q.put((rank, bool(torch.equal(local, glob[rows]))))
+    tdist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_halo_exchange_gloo(world):
+    import multiprocessing as mp
+    import socket
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    ps = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in ps:
+        p.start()
+    res = dict(q.get(timeout=120) for _ in range(world))
+    for p in ps:
+        p.join(timeout=60)
+    assert all(res[r] for r in range(world))

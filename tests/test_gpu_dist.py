@@ -1,0 +1,31 @@
+"""z-slab partition on one GPU: each rank's conv on (own + halo) rows,
+outputs for own rows only (t2sc_coords_create_halo), equals the global conv
+on those rows. The NCCL exchange itself is covered by the gloo test and
+by bench.py under torchrun."""
+import ctypes
+
+import numpy as np
+import pytest
+
+from _cases import F16_TOL, conv_inputs, rel_err
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("world,dtype", [(2, "bf16"), (4, "bf16"), (3, "f32")])
+def test_slabs_equal_global_conv(t2sc, world, dtype):
+    from t2sc import _lib, dist
+    S = t2sc.synth
+    ctx = t2sc.Context.default(0)
+    coords = S.shell(*S.SHELLS["cfg1"])
+    x, w, b = conv_inputs(S, len(coords), 64, 64, seed=77)
+    conv = t2sc.SparseConv3d(w, b, dtype=dtype, ctx=ctx)
+    ref = conv.forward(t2sc.SparseTensor(x, coords, ctx=ctx), silu=True).feats
+    for sl in dist.partition(coords, world):
+        rows = sl.rows
+        c = t2sc.Coords(ctx, coords[rows], n_targets=sl.n_own)
+        y = np.empty((sl.n_own, 64), np.float32)
+        xl = np.ascontiguousarray(x[rows])
+        _lib.check(_lib.lib.t2sc_conv_forward(conv.handle, c.handle, xl.ctypes.data_as(ctypes.c_void_p),
+                                              y.ctypes.data_as(ctypes.c_void_p), _lib.SILU, None), ctx.handle)
+        assert rel_err(y, ref[sl.own]) <= (1e-6 if dtype == "f32" else F16_TOL)

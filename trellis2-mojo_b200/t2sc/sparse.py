@@ -66,10 +66,15 @@ class Context:
 class Coords:
     """Device coordinates + hash + cached neighbour maps (the spatial cache)."""
 
-    def __init__(self, ctx, coords=None, n=None, device_ptr=None):
+    def __init__(self, ctx, coords=None, n=None, device_ptr=None, n_targets=None):
+        """n_targets: only the first n_targets rows receive conv outputs; the
+        rest are halo rows that act as sources (t2sc_coords_create_halo)."""
         self.ctx = ctx
         h = ctypes.c_void_p()
-        if device_ptr is not None:
+        if n_targets is not None:
+            coords = np.ascontiguousarray(coords, dtype=np.int32)
+            rc = lib.t2sc_coords_create_halo(ctx.handle, _p(coords), coords.shape[0], n_targets, 0, ctypes.byref(h))
+        elif device_ptr is not None:
             rc = lib.t2sc_coords_create_device(ctx.handle, ctypes.c_void_p(device_ptr), n, ctypes.byref(h))
         else:
             coords = np.ascontiguousarray(coords, dtype=np.int32)
