@@ -107,6 +107,13 @@ int t2sc_ctx_create(int device, t2sc_ctx **out) {
     ctx->device = device;
     ctx->num_sms = prop.multiProcessorCount;
     if (cudaStreamCreateWithFlags(&ctx->own_stream, cudaStreamNonBlocking) != cudaSuccess) return T2SC_ERR_CUDA;
+    // keep the device's stream-ordered pool warm: scratch freed by one call
+    // is reused by the next instead of being unmapped at every synchronise
+    cudaMemPool_t pool;
+    if (cudaDeviceGetDefaultMemPool(&pool, device) == cudaSuccess) {
+      uint64_t keep = UINT64_MAX;
+      cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep);
+    }
     ctx->stream = ctx->own_stream;
     if (cudaMalloc((void **)&ctx->d_err, sizeof(int)) != cudaSuccess) return T2SC_ERR_OOM;
     if (cudaMemset(ctx->d_err, 0, sizeof(int)) != cudaSuccess) return T2SC_ERR_CUDA;

@@ -45,6 +45,10 @@
 #include "internal.h"
 #include "sm100.cuh"
 
+#ifndef T2SC_COPY_WARPS_128
+#define T2SC_COPY_WARPS_128 8
+#endif
+
 namespace t2sc {
 namespace {
 
@@ -58,9 +62,10 @@ constexpr int kCopyWarp0 = 4;
 // Warp roles: 0-3 epilogue; kCopyWarps copy warps (8 in the 16-bit modes,
 // 4 in the split-TF32 mode, whose epilogue needs the registers); one
 // control warp (weight copies, index prefetch); one MMA warp.
-template <int DT>
+template <int DT, int RB = 128>
 struct Roles {
-  static constexpr int kCopyWarps = DT == 3 ? 4 : 8;
+  // 16-byte vectors per row: each warp must own >= 32 / (RB / 16) rows
+  static constexpr int kCopyWarps = DT == 3 ? 4 : (RB == 128 ? T2SC_COPY_WARPS_128 : 8);
   static constexpr int kControlWarp = kCopyWarp0 + kCopyWarps;
   static constexpr int kMmaWarp = kControlWarp + 1;
   static constexpr int kThreads = 32 * (kMmaWarp + 1);
@@ -170,15 +175,18 @@ __device__ __forceinline__ void store16(const TcArgs &a, int orow, int col, cons
   yp[1] = o1;
 }
 
-// Warp-uniform bounded wait: lane 0 polls, the verdict is broadcast.
+// Warp-uniform bounded wait: every lane probes the barrier (the common
+// case, an already completed phase, costs one probe); a lane that has to
+// wait falls into the bounded loop; the verdict is agreed with a vote.
 __device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, volatile int *abort, int *err) {
-  int ok = 1;
-  if ((threadIdx.x & 31) == 0) ok = sm100::mbar_wait_bounded(bar, parity, abort, err, kDevErrTimeout, kWaitLimit);
-  return __shfl_sync(0xffffffffu, ok, 0) != 0;
+  bool ok = sm100::mbar_test_wait(bar, parity);
+  if (__all_sync(0xffffffffu, ok)) return true;
+  if (!ok) ok = sm100::mbar_wait_bounded(bar, parity, abort, err, kDevErrTimeout, kWaitLimit);
+  return __all_sync(0xffffffffu, ok);
 }
 
 template <int DT, int RB>
-__global__ void __launch_bounds__(Roles<DT>::kThreads, 1)
+__global__ void __launch_bounds__(Roles<DT, RB>::kThreads, 1)
     conv_tc_kernel(const TcArgs a) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // 1024-byte alignment for the swizzle atoms
@@ -196,7 +204,7 @@ __global__ void __launch_bounds__(Roles<DT>::kThreads, 1)
   const uint32_t idxf0 = mma_done + 8, idxe0 = idxf0 + 16;
 
   constexpr bool kSplit = DT == kModeTf32x3;
-  constexpr int kW = Roles<DT>::kCopyWarps, kControlWarp = Roles<DT>::kControlWarp, kMmaWarp = Roles<DT>::kMmaWarp;
+  constexpr int kW = Roles<DT, RB>::kCopyWarps, kControlWarp = Roles<DT, RB>::kControlWarp, kMmaWarp = Roles<DT, RB>::kMmaWarp;
   constexpr int ES = kSplit ? 4 : 2;   // element bytes
   constexpr int BKE = RB / ES;         // elements per chunk row
   const uint32_t a_tile = kTileRows * RB, b_tile = (uint32_t)a.bn * RB;
@@ -598,7 +606,7 @@ int launch_tc(t2sc_conv *cv, const TcArgs &args, int grid, size_t smem, std::str
     const size_t bytes = 10 * kTraceN * sizeof(long long);
     T2SC_CUDA(cudaMalloc((void **)&t.trace, bytes), "trace");
     T2SC_CUDA(cudaMemset(t.trace, 0, bytes), "trace");
-    kfn<<<grid, Roles<DT>::kThreads, smem, cv->ctx->stream>>>(t);
+    kfn<<<grid, Roles<DT, RB>::kThreads, smem, cv->ctx->stream>>>(t);
     T2SC_LAUNCHED(cv->ctx, "conv_tc");
     std::vector<long long> h(10 * kTraceN);
     T2SC_CUDA(cudaMemcpyAsync(h.data(), t.trace, bytes, cudaMemcpyDeviceToHost, cv->ctx->stream), "trace");
@@ -610,7 +618,7 @@ int launch_tc(t2sc_conv *cv, const TcArgs &args, int grid, size_t smem, std::str
     }
     return T2SC_OK;
   }
-  kfn<<<grid, Roles<DT>::kThreads, smem, cv->ctx->stream>>>(args);
+  kfn<<<grid, Roles<DT, RB>::kThreads, smem, cv->ctx->stream>>>(args);
   T2SC_LAUNCHED(cv->ctx, "conv_tc");
   return T2SC_OK;
 }

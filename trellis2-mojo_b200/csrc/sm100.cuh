@@ -50,6 +50,20 @@ __device__ __forceinline__ bool mbar_test_wait(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
+// Blocking probe: the thread may sleep (up to the hint, in ns) until the
+// phase completes instead of spinning on issue slots the working warps need.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "r"(1000000u)
+      : "memory");
+  return ok != 0;
+}
+
 // Bounded wait: polls until the phase with `parity` completes, another
 // role raised `abort`, or ~`limit_cycles` SM clocks pass (then it raises
 // abort and ORs `err_bit` into *err). Returns false when it gave up.
@@ -58,8 +72,8 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity,
   if (mbar_test_wait(bar, parity)) return true;
   long long t0 = clock64();
   for (uint32_t i = 1;; i++) {
-    if (mbar_test_wait(bar, parity)) return true;
-    if ((i & 255) == 0) {
+    if (mbar_try_wait_sleep(bar, parity)) return true;
+    if ((i & 3) == 0) {
       if (*abort) return false;
       if (clock64() - t0 > limit_cycles) {
         *abort = 1;
@@ -80,7 +94,9 @@ __device__ __forceinline__ bool mbar_wait_cycles(uint32_t bar, uint32_t parity, 
 
 // ---- cp.async (Ampere-style, zero-filling when src_bytes == 0) ----
 __device__ __forceinline__ void cp_async_16(uint32_t dst, const void *src, uint32_t src_bytes) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
+  // no "memory" clobber: the copy's completion is ordered by the mbarrier
+  // arrive that follows it, and the address math around it may interleave
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes));
 }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 template <int N>
