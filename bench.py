@@ -372,6 +372,24 @@ def run_distributed(args):
         step()
     ctx.synchronize()
     torch.cuda.synchronize()
+    # The step (4 x (halo exchange + conv)) is captured once in a CUDA graph:
+    # at 4-8 ranks a layer is ~20 us of GPU work, less than the host needs
+    # to issue it eagerly. Falls back to eager launches if capture fails.
+    graph = g = None
+    launches_per_step = len(convs)
+    try:
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            step()
+        torch.cuda.synchronize()
+        g.replay()
+        torch.cuda.synchronize()
+        graph = g
+    except Exception as exc:  # noqa: BLE001
+        if rank == 0:
+            print(f"# graph capture failed, timing eager steps: {exc}", file=sys.stderr)
+        torch.cuda.synchronize()
+    run = graph.replay if graph is not None else step
     ev = lambda: torch.cuda.Event(enable_timing=True)  # noqa: E731
     times = []
     launches0 = ctx.launch_count()
@@ -383,15 +401,15 @@ def run_distributed(args):
         tdist.barrier()
         s0, s1 = ev(), ev()
         s0.record(stream)
-        step()
+        run()
         s1.record(stream)
         torch.cuda.synchronize()
         times.append(s0.elapsed_time(s1))
-    launches = ctx.launch_count() - launches0
+    launches = ctx.launch_count() - launches0 if graph is None else launches_per_step * args.steps
     t_load = time.perf_counter()
     while time.perf_counter() - t_load < 1.0:
         for _ in range(10):
-            step()
+            run()
         torch.cuda.synchronize()
     if clk:
         clk.__exit__()
@@ -409,7 +427,8 @@ def run_distributed(args):
         tdist.barrier()
         t0 = time.perf_counter()
         xin[:n_own].copy_(xh.to("cuda", non_blocking=True))
-        out = step()
+        run()
+        out = bufs[(len(convs) - 1) & 1]
         yh.copy_(out[:n_own].float(), non_blocking=True)
         torch.cuda.synchronize()
         if s >= 2:
@@ -427,13 +446,23 @@ def run_distributed(args):
                 "config": {"workload": WORKLOAD, "voxels": n, "edges": E, "layers": LAYERS, "channels": C,
                            "l2": "flushed between steps (256 MiB write)",
                            "parallelism": f"z-slab x{world}, one-voxel halo over NCCL send/recv",
-                           "rank0_rows": n_own, "rank0_halo_rows": n_loc - n_own},
+                           "rank0_rows": n_own, "rank0_halo_rows": n_loc - n_own,
+                           "cuda_graph": graph is not None},
                 "e2e": {"value": flops / e2e_s / 1e12, "unit": UNIT, "h2d_bytes_per_step": n * C * 4,
                         "d2h_bytes_per_step": n * C * 4, "ms_per_step": 1e3 * e2e_s},
                 "gpu_launches": launches, "clocks": clk.summary if clk else None, "cpu_baseline": None}
         print(json.dumps(line))
+    # Release the captured graph (it references the NCCL communicator) before
+    # the final barrier, then leave without tearing the communicators down:
+    # destroying a process group whose NCCL comm was captured in a graph can
+    # block, and the process is done.
+    run = graph = g = None  # noqa: F841
+    torch.cuda.synchronize()
     tdist.barrier()
-    tdist.destroy_process_group()
+    torch.cuda.synchronize()
+    sys.stdout.flush()
+    sys.stderr.flush()
+    os._exit(0)
 
 
 if __name__ == "__main__":

@@ -599,7 +599,15 @@ __global__ void split_tf32_kernel(const float4 *__restrict__ x, float4 *__restri
 template <int DT, int RB>
 int launch_tc(t2sc_conv *cv, const TcArgs &args, int grid, size_t smem, std::string &err) {
   auto kfn = conv_tc_kernel<DT, RB>;
-  T2SC_CUDA(cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem), "tc smem attr");
+  // set the shared-memory opt-in once per instantiation and size (a host-only
+  // call kept out of the per-launch path, e.g. during stream capture)
+  static int attr_smem[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64 || attr_smem[dev] < (int)smem) {
+    T2SC_CUDA(cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem), "tc smem attr");
+    if (dev >= 0 && dev < 64) attr_smem[dev] = (int)smem;
+  }
   const char *trace_path = getenv("T2SC_CONV_TRACE");
   if (trace_path) {  // diagnostics only: allocates, synchronises and writes a file
     TcArgs t = args;
