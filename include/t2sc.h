@@ -71,6 +71,13 @@ int t2sc_ctx_synchronize(t2sc_ctx *ctx);
 const char *t2sc_last_error(const t2sc_ctx *ctx);
 /* Kernel launches issued by this context since creation (diagnostics). */
 int t2sc_ctx_launch_count(const t2sc_ctx *ctx, int64_t *count);
+/* Device self-test (replaces GpuContext's startup self-test,
+ * trellis2_mojo/gpu/context.mojo:7-12, 139-158): a small compute check plus
+ * a wait on a device barrier that nothing completes, bounded to wait_us
+ * microseconds (1..1e6). T2SC_OK when the compute is right and the bounded
+ * wait came back with its timeout flag (the mechanism every conv pipeline
+ * wait relies on); the context stays usable either way. */
+int t2sc_ctx_selftest(t2sc_ctx *ctx, int wait_us);
 /* Library version string, e.g. "t2sc 0.1 sm_100a". */
 const char *t2sc_version(void);
 

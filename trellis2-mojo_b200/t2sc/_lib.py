@@ -32,6 +32,7 @@ SIGNATURES = {
     "t2sc_last_error": (ctypes.c_char_p, [P]),
     "t2sc_ctx_launch_count": (I32, [P, PI64]),
     "t2sc_version": (ctypes.c_char_p, []),
+    "t2sc_ctx_selftest": (I32, [P, I32]),
     "t2sc_coords_create": (I32, [P, P, I64, PP]),
     "t2sc_coords_create_device": (I32, [P, P, I64, PP]),
     "t2sc_coords_create_halo": (I32, [P, P, I64, I64, I32, PP]),

@@ -45,6 +45,10 @@ class Context:
             cls._default[device] = cls(device)
         return cls._default[device]
 
+    def selftest(self, wait_us=2000):
+        """Compute check + a bounded device wait that must time out cleanly."""
+        check(lib.t2sc_ctx_selftest(self.handle, wait_us), self.handle)
+
     def synchronize(self):
         check(lib.t2sc_ctx_synchronize(self.handle), self.handle)
 
