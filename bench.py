@@ -180,6 +180,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="t2sc", choices=["t2sc", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--overlap", action="store_true",
+                    help="N>1: convolve interior rows while the halo is in flight (measured slower at N=4 and 8: "
+                         "the second launch per layer costs more than the hidden exchange)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -342,10 +345,16 @@ def run_distributed(args):
     rows = slab.rows
     n_own, n_loc = slab.n_own, len(rows)
     convs = [t2sc.SparseConv3d(w, b, dtype="bf16", ctx=ctx) for w, b in zip(ws, bs)]
-    cdev = t2sc.Coords(ctx, coords[rows], n_targets=n_own)
+    n_int = slab.n_int
+    # interior targets [0, n_int) need no halo; boundary targets [n_int, n_own) do
+    c_int = t2sc.Coords(ctx, coords[rows], targets=(0, n_int))
+    c_bnd = t2sc.Coords(ctx, coords[rows], targets=(n_int, n_own))
+    c_all = t2sc.Coords(ctx, coords[rows], n_targets=n_own) if (not args.overlap) else None
     torch.cuda.synchronize()
     t0 = time.perf_counter()
-    e_loc = cdev.build_map()
+    e_loc = c_int.build_map() + c_bnd.build_map()
+    if c_all is not None:
+        c_all.build_map()
     torch.cuda.synchronize()
     map_ms = 1e3 * (time.perf_counter() - t0)
     e_all = torch.tensor([e_loc], dtype=torch.int64, device="cuda")
@@ -361,10 +370,24 @@ def run_distributed(args):
     def step():
         cur = xin
         for i, cv in enumerate(convs):
-            dist.exchange_halo(cur, slab, tdist)  # halo rows of this layer's input
+            pending = dist.start_halo(cur, slab, tdist)  # halo rows of this layer's input
             out = bufs[i & 1]
-            _lib.check(L.t2sc_conv_forward_device(cv.handle, cdev.handle, ctypes.c_void_p(cur.data_ptr()),
+            if (not args.overlap):
+                for q in pending:
+                    q.wait()
+                _lib.check(L.t2sc_conv_forward_device(cv.handle, c_all.handle, ctypes.c_void_p(cur.data_ptr()),
+                                                      ctypes.c_void_p(out.data_ptr()), _lib.SILU, None), ctx.handle)
+                cur = out
+                continue
+            # interior rows while the halo is in flight, boundary rows after it lands
+            _lib.check(L.t2sc_conv_forward_device(cv.handle, c_int.handle, ctypes.c_void_p(cur.data_ptr()),
                                                   ctypes.c_void_p(out.data_ptr()), _lib.SILU, None), ctx.handle)
+            for q in pending:
+                q.wait()
+            if n_own > n_int:
+                _lib.check(L.t2sc_conv_forward_device(
+                    cv.handle, c_bnd.handle, ctypes.c_void_p(cur.data_ptr()),
+                    ctypes.c_void_p(out.data_ptr() + n_int * C * out.element_size()), _lib.SILU, None), ctx.handle)
             cur = out
         return cur
 
@@ -376,7 +399,7 @@ def run_distributed(args):
     # at 4-8 ranks a layer is ~20 us of GPU work, less than the host needs
     # to issue it eagerly. Falls back to eager launches if capture fails.
     graph = g = None
-    launches_per_step = len(convs)
+    launches_per_step = len(convs) * (2 if n_own > n_int and not (not args.overlap) else 1)
     try:
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g, stream=stream):
@@ -445,7 +468,8 @@ def run_distributed(args):
                 "mvoxel_per_s": LAYERS * n / (ms * 1e-3) / 1e6, "map_build_ms": map_ms,
                 "config": {"workload": WORKLOAD, "voxels": n, "edges": E, "layers": LAYERS, "channels": C,
                            "l2": "flushed between steps (256 MiB write)",
-                           "parallelism": f"z-slab x{world}, one-voxel halo over NCCL send/recv",
+                           "parallelism": f"z-slab x{world}, one-voxel halo over NCCL send/recv"
+                                          + (" overlapped with the interior rows' conv" if args.overlap else ""),
                            "rank0_rows": n_own, "rank0_halo_rows": n_loc - n_own,
                            "cuda_graph": graph is not None},
                 "e2e": {"value": flops / e2e_s / 1e12, "unit": UNIT, "h2d_bytes_per_step": n * C * 4,

@@ -94,6 +94,14 @@ int t2sc_coords_create_device(t2sc_ctx *ctx, const int32_t *coords_dev, int64_t 
  * pointer. New interface (the reference has no partitioned path). */
 int t2sc_coords_create_halo(t2sc_ctx *ctx, const int32_t *coords, int64_t n, int64_t n_targets,
                             int on_device, t2sc_coords **out);
+/* General form: target rows are [target_begin, target_end) of the n rows;
+ * every row is a source. Conv outputs (and residuals) are indexed by target
+ * row - target_begin, so a caller that keeps one [n, C] output buffer
+ * passes y + target_begin * C. Exported edge lists use the same target
+ * numbering. Lets a rank convolve its interior rows while the halo of its
+ * boundary rows is still in flight. New interface (no reference counterpart). */
+int t2sc_coords_create_range(t2sc_ctx *ctx, const int32_t *coords, int64_t n, int64_t target_begin,
+                             int64_t target_end, int on_device, t2sc_coords **out);
 int t2sc_coords_destroy(t2sc_coords *c);
 /* Number of target rows (= all rows unless created with halo rows). */
 int t2sc_coords_count(const t2sc_coords *c, int64_t *n);

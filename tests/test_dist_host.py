@@ -38,6 +38,11 @@ def test_partition_neighbourhoods_complete(t2sc, oracle, world):
         if r < world - 1:
             assert np.array_equal(s.halo_hi, slabs[r + 1].own[slabs[r + 1].lo_send])
     _local_map_matches_global(oracle, coords, slabs)
+    # interior rows (first n_int) have no neighbour among the halo rows
+    for sl in slabs:
+        rows = sl.rows
+        ls, lt, lk = oracle.neighbor_map(coords[rows])
+        assert not np.any((lt < sl.n_int) & (ls >= sl.n_own))
 
 
 def test_partition_rejects_too_thin(t2sc):

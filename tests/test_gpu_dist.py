@@ -29,3 +29,14 @@ def test_slabs_equal_global_conv(t2sc, world, dtype):
         _lib.check(_lib.lib.t2sc_conv_forward(conv.handle, c.handle, xl.ctypes.data_as(ctypes.c_void_p),
                                               y.ctypes.data_as(ctypes.c_void_p), _lib.SILU, None), ctx.handle)
         assert rel_err(y, ref[sl.own]) <= (1e-6 if dtype == "f32" else F16_TOL)
+        # interior and boundary target ranges computed separately fill the same rows
+        y2 = np.empty((sl.n_own, 64), np.float32)
+        for t0, t1 in ((0, sl.n_int), (sl.n_int, sl.n_own)):
+            if t1 == t0:
+                continue
+            cr = t2sc.Coords(ctx, coords[rows], targets=(t0, t1))
+            part = np.empty((t1 - t0, 64), np.float32)
+            _lib.check(_lib.lib.t2sc_conv_forward(conv.handle, cr.handle, xl.ctypes.data_as(ctypes.c_void_p),
+                                                  part.ctypes.data_as(ctypes.c_void_p), _lib.SILU, None), ctx.handle)
+            y2[t0:t1] = part
+        assert rel_err(y2, ref[sl.own]) <= (1e-6 if dtype == "f32" else F16_TOL)

@@ -155,11 +155,12 @@ int t2sc_ctx_launch_count(const t2sc_ctx *ctx, int64_t *count) {
 // ------------------------------- coordinates -------------------------------
 
 static int coords_create_impl(t2sc_ctx *ctx, const int32_t *coords, int64_t n, int64_t n_targets, bool on_device,
-                              t2sc_coords **out) {
+                              t2sc_coords **out, int64_t target_begin = 0) {
   if (!ctx || !out) return T2SC_ERR_INVALID;
   *out = nullptr;
   if (n < 0 || (n > 0 && !coords)) return fail(ctx, T2SC_ERR_INVALID, "coords: bad pointer or count");
-  if (n_targets < 0 || n_targets > n) return fail(ctx, T2SC_ERR_INVALID, "coords: n_targets must be in [0, n]");
+  if (target_begin < 0 || n_targets < 0 || target_begin + n_targets > n)
+    return fail(ctx, T2SC_ERR_INVALID, "coords: target rows must lie in [0, n)");
   if (n >= (int64_t(1) << 31)) return fail(ctx, T2SC_ERR_UNSUPPORTED, "coords: more than 2^31-1 rows");
   return guarded(ctx, [&]() -> int {
     DeviceGuard g(ctx->device);
@@ -168,6 +169,7 @@ static int coords_create_impl(t2sc_ctx *ctx, const int32_t *coords, int64_t n, i
     c->ctx = ctx;
     c->n = n;
     c->n_targets = n_targets;
+    c->target_begin = target_begin;
     T2SC_CUDA(cudaMalloc((void **)&c->d_coords, (size_t)(n > 0 ? n : 1) * 16), "coords");
     if (n > 0)
       T2SC_CUDA(cudaMemcpyAsync(c->d_coords, coords, (size_t)n * 16,
@@ -192,6 +194,11 @@ int t2sc_coords_create_device(t2sc_ctx *ctx, const int32_t *coords, int64_t n, t
 int t2sc_coords_create_halo(t2sc_ctx *ctx, const int32_t *coords, int64_t n, int64_t n_targets, int on_device,
                             t2sc_coords **out) {
   return coords_create_impl(ctx, coords, n, n_targets, on_device != 0, out);
+}
+
+int t2sc_coords_create_range(t2sc_ctx *ctx, const int32_t *coords, int64_t n, int64_t target_begin,
+                             int64_t target_end, int on_device, t2sc_coords **out) {
+  return coords_create_impl(ctx, coords, n, target_end - target_begin, on_device != 0, out, target_begin);
 }
 
 int t2sc_coords_destroy(t2sc_coords *c) {
@@ -413,7 +420,8 @@ int t2sc_conv_chain_forward(t2sc_conv *const *convs, int n_layers, t2sc_coords *
       cmax = convs[i]->co > cmax ? convs[i]->co : cmax;
     }
     const int64_t n = c->n;
-    if (c->n_targets != n) return fail(ctx, T2SC_ERR_INVALID, "chain: coordinates with halo rows are not chainable");
+    if (c->n_targets != n || c->target_begin != 0)
+      return fail(ctx, T2SC_ERR_INVALID, "chain: coordinates with halo rows are not chainable");
     if (n == 0) return T2SC_OK;
     if (!x || !y) return fail(ctx, T2SC_ERR_INVALID, "null feature buffer");
     DevBuf din, b0, b1;

@@ -242,7 +242,7 @@ int build_map(t2sc_coords *c, int kd, int kh, int kw, int dil, t2sc_map **out, s
     size_t temp_bytes = 0;
     T2SC_CUDA(cudaMallocAsync((void **)&d_e, sizeof(unsigned long long), st), "map scratch");
     T2SC_CUDA(cudaMemsetAsync(d_e, 0, sizeof(unsigned long long), st), "map scratch");
-    neighbor_map_kernel<<<nblk(n, 128), 128, 0, st>>>((const int4 *)c->d_coords, n, c->d_keys, c->d_vals,
+    neighbor_map_kernel<<<nblk(n, 128), 128, 0, st>>>((const int4 *)c->d_coords + c->target_begin, n, c->d_keys, c->d_vals,
                                                        c->hcap - 1, kd, kh, kw, dil, m->nbr, m->mask, d_e);
     T2SC_LAUNCHED(ctx, "neighbor_map");
     T2SC_CUDA(cudaMallocAsync((void **)&mask_sorted, sizeof(uint32_t) * n, st), "sort scratch");

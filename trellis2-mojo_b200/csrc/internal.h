@@ -61,6 +61,7 @@ struct t2sc_coords {
   t2sc_ctx *ctx = nullptr;
   int64_t n = 0;                 // all rows (targets first, then halo rows)
   int64_t n_targets = 0;         // rows that receive conv outputs
+  int64_t target_begin = 0;      // first target row (targets are rows [target_begin, +n_targets))
   int32_t *d_coords = nullptr;   // [n,4]
   uint64_t hcap = 0;             // hash capacity (power of two)
   int64_t *d_keys = nullptr;     // [hcap]

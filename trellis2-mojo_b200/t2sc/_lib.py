@@ -36,6 +36,7 @@ SIGNATURES = {
     "t2sc_coords_create": (I32, [P, P, I64, PP]),
     "t2sc_coords_create_device": (I32, [P, P, I64, PP]),
     "t2sc_coords_create_halo": (I32, [P, P, I64, I64, I32, PP]),
+    "t2sc_coords_create_range": (I32, [P, P, I64, I64, I64, I32, PP]),
     "t2sc_coords_destroy": (I32, [P]),
     "t2sc_coords_count": (I32, [P, PI64]),
     "t2sc_coords_build_map": (I32, [P, I32, I32, I32, I32, PI64]),

@@ -9,10 +9,13 @@ below z_lo and above z_hi - 1 (depth = dilation * (kernel // 2); 1 for the
 only (t2sc_coords_create_halo) equals the global conv restricted to the
 rank's rows, because every neighbour of an own row is own or halo.
 
-Local row order, chosen so that every exchange is a contiguous slice:
-    [own rows in the low boundary planes | interior | own rows in the high
+Local row order, chosen so that every exchange is a contiguous slice and
+the rows that need no halo come first:
+    [interior | own rows in the low boundary planes | own rows in the high
      boundary planes | halo from below | halo from above]
-Own rows keep their global (lexicographic) order inside each group.
+Own rows keep their global (lexicographic) order inside each group. A layer
+can then convolve the interior rows (targets [0, n_int)) while the halo is
+in flight, and the boundary rows (targets [n_int, n_own)) after it lands.
 """
 import numpy as np
 
@@ -22,11 +25,13 @@ class Slab:
 
     def __init__(self, rank, world, z_lo, z_hi, own, lo_send, hi_send, halo_lo, halo_hi):
         self.rank, self.world, self.z_lo, self.z_hi = rank, world, z_lo, z_hi
-        self.own = own            # global rows, local order (boundary-low, interior, boundary-high)
+        self.own = own            # global rows, local order (interior, boundary-low, boundary-high)
         self.lo_send = lo_send    # slice of own rows sent to rank - 1
         self.hi_send = hi_send    # slice of own rows sent to rank + 1
         self.halo_lo = halo_lo    # global rows received from rank - 1 (its hi_send, same order)
         self.halo_hi = halo_hi    # global rows received from rank + 1 (its lo_send, same order)
+        self.n_int = lo_send.start if lo_send.stop > lo_send.start else (
+            hi_send.start if hi_send.stop > hi_send.start else len(own))  # interior rows come first
 
     @property
     def n_own(self):
@@ -74,9 +79,10 @@ def partition(coords, world, depth=1):
         zr = z[rows]
         in_lo = (zr < lo + depth) if r > 0 else np.zeros(len(rows), bool)
         in_hi = (zr >= hi - depth) if r < world - 1 else np.zeros(len(rows), bool)
-        own = np.concatenate([rows[in_lo], rows[~in_lo & ~in_hi], rows[in_hi]])
-        n_lo, n_hi = int(in_lo.sum()), int(in_hi.sum())
-        parts.append((lo, hi, own, slice(0, n_lo), slice(len(own) - n_hi, len(own))))
+        interior = rows[~in_lo & ~in_hi]
+        own = np.concatenate([interior, rows[in_lo], rows[in_hi]])
+        n_int, n_lo, n_hi = len(interior), int(in_lo.sum()), int(in_hi.sum())
+        parts.append((lo, hi, own, slice(n_int, n_int + n_lo), slice(n_int + n_lo, n_int + n_lo + n_hi)))
     slabs = []
     for r in range(world):
         lo, hi, own, lo_send, hi_send = parts[r]
@@ -86,11 +92,9 @@ def partition(coords, world, depth=1):
     return slabs
 
 
-def exchange_halo(feats, slab, dist):
-    """Fill the halo rows of `feats` [n_own + n_halo, C] (a torch tensor on
-    any backend torch.distributed supports) from the z-neighbours: rank r
-    sends its low boundary rows to r - 1 and its high boundary rows to
-    r + 1, as one grouped batch (ncclGroupStart/End under NCCL)."""
+def start_halo(feats, slab, dist):
+    """Issue the halo exchange of `feats` (see exchange_halo) and return the
+    pending work; wait on it before reading the halo rows."""
     n_own, nlo = slab.n_own, len(slab.halo_lo)
     r, w = slab.rank, slab.world
     ops = []
@@ -100,6 +104,13 @@ def exchange_halo(feats, slab, dist):
     if r < w - 1:
         ops.append(dist.P2POp(dist.isend, feats[slab.hi_send], r + 1))
         ops.append(dist.P2POp(dist.irecv, feats[n_own + nlo:], r + 1))
-    if ops:
-        for q in dist.batch_isend_irecv(ops):
-            q.wait()
+    return dist.batch_isend_irecv(ops) if ops else []
+
+
+def exchange_halo(feats, slab, dist):
+    """Fill the halo rows of `feats` [n_own + n_halo, C] (a torch tensor on
+    any backend torch.distributed supports) from the z-neighbours: rank r
+    sends its low boundary rows to r - 1 and its high boundary rows to
+    r + 1, as one grouped batch (ncclGroupStart/End under NCCL)."""
+    for q in start_halo(feats, slab, dist):
+        q.wait()

@@ -70,12 +70,16 @@ class Context:
 class Coords:
     """Device coordinates + hash + cached neighbour maps (the spatial cache)."""
 
-    def __init__(self, ctx, coords=None, n=None, device_ptr=None, n_targets=None):
+    def __init__(self, ctx, coords=None, n=None, device_ptr=None, n_targets=None, targets=None):
         """n_targets: only the first n_targets rows receive conv outputs; the
         rest are halo rows that act as sources (t2sc_coords_create_halo)."""
         self.ctx = ctx
         h = ctypes.c_void_p()
-        if n_targets is not None:
+        if targets is not None:  # target rows [t0, t1); all rows are sources
+            coords = np.ascontiguousarray(coords, dtype=np.int32)
+            rc = lib.t2sc_coords_create_range(ctx.handle, _p(coords), coords.shape[0], int(targets[0]), int(targets[1]),
+                                              0, ctypes.byref(h))
+        elif n_targets is not None:
             coords = np.ascontiguousarray(coords, dtype=np.int32)
             rc = lib.t2sc_coords_create_halo(ctx.handle, _p(coords), coords.shape[0], n_targets, 0, ctypes.byref(h))
         elif device_ptr is not None:
