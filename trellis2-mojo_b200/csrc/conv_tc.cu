@@ -57,6 +57,11 @@ constexpr int kMinStages = 3;
 constexpr int kTf32MaxBn = 128;                  // register-resident partial sums per row
 constexpr long long kWaitLimit = 4000000000LL;  // ~2 s of SM clocks
 constexpr int kSmemMax = 232448;  // 227 KB: the sm_100 per-block dynamic shared memory limit
+constexpr int kSmemHalf = 115712;  // per block when two share an SM's 228 KB (1 KB reserved each)
+#ifndef T2SC_CTAS_PER_SM
+#define T2SC_CTAS_PER_SM 2
+#endif
+constexpr int kDefaultCtasPerSm = T2SC_CTAS_PER_SM;
 constexpr int kModeTf32x3 = 3;    // beside T2SC_DT_F16 (1) and T2SC_DT_BF16 (2)
 constexpr int kCopyWarp0 = 4;
 // Warp roles: 0-3 epilogue; kCopyWarps copy warps (8 in the 16-bit modes,
@@ -737,7 +742,16 @@ int conv_tc_launch(t2sc_conv *cv, t2sc_map *m, const void *x, void *y, int flags
   a.b_bytes = (uint32_t)cv->bn * cv->row_bytes * na;
   a.sub_bytes = (a.a_bytes + a.b_bytes + 1023u) & ~1023u;
   const int idx_bytes = 2 * kMaxK * kTileRows * 4;  // double-buffered tile index blocks
-  const int avail = kSmemMax - idx_bytes - 1280;
+  // CTAs per SM: 2 independent pipelines when both fit (TMEM <= 256 columns
+  // each, half the shared memory each), else 1.
+  static const int ctas_env = [] {
+    const char *e = getenv("T2SC_CONV_CTAS");
+    return e ? atoi(e) : kDefaultCtasPerSm;
+  }();
+  int ctas = (ctas_env >= 2 && cols <= 256 && cv->dtype != T2SC_DT_F32) ? 2 : 1;
+  // two CTAs only when half the shared memory still holds kMinStages stages
+  if (ctas == 2 && (int)(kSmemHalf - idx_bytes - 1280) / (int)a.sub_bytes < kMinStages) ctas = 1;
+  const int avail = (ctas == 2 ? kSmemHalf : kSmemMax) - idx_bytes - 1280;
   // Small pairs are grouped so that one stage carries up to ~48 KB: the
   // per-stage handshake is then paid once per several MMA k-steps.
   // Split-TF32 drains per offset, so it keeps one pair per stage.
@@ -753,12 +767,13 @@ int conv_tc_launch(t2sc_conv *cv, t2sc_map *m, const void *x, void *y, int flags
     return T2SC_ERR_UNSUPPORTED;
   }
   a.stages = S;
-  // stages + index blocks + barriers/slots + alignment slack; never below
-  // 120 KB so that a single CTA owns each SM (and its TMEM).
+  // stages + index blocks + barriers/slots + alignment slack; with one CTA
+  // per SM never below 120 KB, so that it alone owns the SM (and its TMEM).
   size_t smem = (size_t)S * a.stage_bytes + idx_bytes + 256 + 1024;
-  if (smem < 120 * 1024) smem = 120 * 1024;
+  if (ctas == 1 && smem < 120 * 1024) smem = 120 * 1024;
   const int64_t nunits = (int64_t)a.ntiles * a.nco_tiles;
-  const int grid = (int)(nunits < cv->ctx->num_sms ? nunits : cv->ctx->num_sms);
+  const int64_t slots = (int64_t)cv->ctx->num_sms * ctas;
+  const int grid = (int)(nunits < slots ? nunits : slots);
   if (cv->dtype == T2SC_DT_F32) {
     // split x into TF32 hi/lo parts in stream-ordered scratch
     cudaStream_t st = cv->ctx->stream;
