@@ -182,6 +182,17 @@ int t2sc_subdivide_noalloc_device(t2sc_ctx *ctx, const int32_t *coords, int64_t 
                                   int32_t *out_coords, void *out_feats, int32_t *out_parent,
                                   int32_t *out_subidx, int64_t *m);
 
+/* ---- LayerNorm (+ SiLU) over the channel dim of device features ----
+ * Replaces LayerNorm32.forward (trellis2_mojo/modules/nn.mojo:313-370) and,
+ * with flags & T2SC_SILU, the activation(..., ACT_SILU) that follows it in
+ * the decoder's upsample block (models/sc_vaes/sparse_unet_vae.mojo:118,123).
+ * x, y: device [rows, c] of dtype (y may alias x); w, b: device f32 [c],
+ * both NULL for affine=False. Per row: mean, population variance,
+ * y = (x - mean) / sqrt(var + eps) (* w + b), then y / (1 + exp(-y)) for
+ * SiLU; statistics in f32. 1 <= c <= 1024. Asynchronous on the stream. */
+int t2sc_layernorm_device(t2sc_ctx *ctx, const void *x, void *y, int64_t rows, int c, const float *w,
+                          const float *b, float eps, int flags, int dtype);
+
 /* ---- synthetic inputs (seeded shells of the benchmark configurations) ----
  * Active cells of a G^3 grid with | |p-c| - R(1 + 0.1 sin(3t) cos(2(f+phase))) | <= h,
  * c = G/2, t = acos((p_z-c)/|p-c|), f = atan2(p_y-c, p_x-c), phase = 0 for

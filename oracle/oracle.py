@@ -49,6 +49,8 @@ def lib():
         L.orc_add.argtypes = [P, P, I64]
         L.orc_round16.restype = None
         L.orc_round16.argtypes = [P, I64, I]
+        L.orc_layernorm.restype = None
+        L.orc_layernorm.argtypes = [P, I64, I, P, P, ctypes.c_float, I, P]
         L.orc_subdivide.restype = I64
         L.orc_subdivide.argtypes = [P, I64, P, I, P, P, P]
         L.orc_select_rows.restype = None
@@ -143,4 +145,13 @@ def c2s_unfold(x, idx, subidx):
     out = np.empty((len(idx), cout), np.float32)
     lib().orc_c2s_unfold(_p(x), cout, _p(np.ascontiguousarray(idx, np.int64)),
                          _p(np.ascontiguousarray(subidx, np.int64)), len(idx), _p(out))
+    return out
+
+
+def layernorm(x, w=None, b=None, eps=1e-6, silu=False):
+    x = np.ascontiguousarray(x, np.float32)
+    out = np.empty_like(x)
+    w = None if w is None else np.ascontiguousarray(w, np.float32)
+    b = None if b is None else np.ascontiguousarray(b, np.float32)
+    lib().orc_layernorm(_p(x), x.shape[0], x.shape[1], _p(w), _p(b), eps, int(silu), _p(out))
     return out

@@ -297,3 +297,45 @@ void orc_c2s_unfold(const float *x, int cout, const int64_t *idx,
     memcpy(out + e * cout, x + slot * cout, sizeof(float) * cout);
   }
 }
+
+static float reduce8(const float *a) { /* SIMD.reduce_add as the halving tree */
+  float t4[4], t2[2];
+  for (int l = 0; l < 4; l++) t4[l] = a[l] + a[l + 4];
+  for (int l = 0; l < 2; l++) t2[l] = t4[l] + t4[l + 2];
+  return t2[0] + t2[1];
+}
+
+void orc_layernorm(const float *x, int64_t rows, int c, const float *w, const float *b, float eps, int silu,
+                   float *out) {
+  for (int64_t r = 0; r < rows; r++) { /* nn.mojo:324-369 */
+    const float *xr = x + r * c;
+    float *orow = out + r * c;
+    float s[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    int i = 0;
+    for (; i + 8 <= c; i += 8)
+      for (int l = 0; l < 8; l++) s[l] += xr[i + l];
+    float mean = reduce8(s);
+    for (; i < c; i++) mean += xr[i];
+    mean /= (float)c;
+    float v[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    i = 0;
+    for (; i + 8 <= c; i += 8)
+      for (int l = 0; l < 8; l++) {
+        float d = xr[i + l] - mean;
+        v[l] += d * d;
+      }
+    float var = reduce8(v);
+    for (; i < c; i++) {
+      float d = xr[i] - mean;
+      var += d * d;
+    }
+    var /= (float)c;
+    float inv_std = 1.0f / sqrtf(var + eps);
+    for (i = 0; i < c; i++) {
+      float y = (xr[i] - mean) * inv_std;
+      if (w) y = y * w[i] + b[i];
+      if (silu) y = y / (1.0f + expf(-y));
+      orow[i] = y;
+    }
+  }
+}

@@ -57,6 +57,15 @@ void orc_add(float *a, const float *b, int64_t n);
 /* Round every value to bf16 (mode 2) or f16 (mode 1), round-to-nearest-even. */
 void orc_round16(float *v, int64_t n, int mode);
 
+/* LayerNorm over the last dim (LayerNorm32.forward,
+ * trellis2_mojo/modules/nn.mojo:313-370): 8-lane partial sums + halving-tree
+ * reduce + scalar tail for the mean and the population variance,
+ * inv_std = 1/sqrt(var + eps), optional affine (w, b nullable), then
+ * optional SiLU (silu != 0; the decoder's norm -> activation pairs,
+ * models/sc_vaes/sparse_unet_vae.mojo:118,123). */
+void orc_layernorm(const float *x, int64_t rows, int c, const float *w, const float *b, float eps, int silu,
+                   float *out);
+
 /* Subdivision child list, sparse/spatial/basic.mojo:144-167 and
  * spatial/spatial2channel.mojo:97-116. positive=0: keep sub != 0 (the
  * forward_subdivision test); positive=1: keep sub > 0 (the decoder's

@@ -140,3 +140,30 @@ def test_golden_fixtures(oracle):
         assert np.array_equal(y, g[case + "_y"])
     idx, sidx, nc = oracle.subdivide(g["sub_coords"], g["sub_mask"])
     assert np.array_equal(nc, g["sub_out_coords"]) and np.array_equal(idx, g["sub_idx"])
+
+
+@pytest.mark.parametrize("c,affine,silu,eps", [(64, True, True, 1e-6), (13, False, False, 1e-5), (1024, True, False, 1e-6)])
+def test_layernorm_oracle(oracle, c, affine, silu, eps):
+    """orc_layernorm (nn.mojo:313-370) against the float64 definition."""
+    rng = np.random.default_rng(c)
+    x = (rng.standard_normal((97, c)) * 3 + 1.5).astype(np.float32)
+    w = rng.standard_normal(c).astype(np.float32) if affine else None
+    b = rng.standard_normal(c).astype(np.float32) if affine else None
+    got = oracle.layernorm(x, w, b, eps, silu)
+    xd = x.astype(np.float64)
+    m = xd.mean(1, keepdims=True)
+    v = ((xd - m) ** 2).mean(1, keepdims=True)
+    ref = (xd - m) / np.sqrt(v + eps)
+    if affine:
+        ref = ref * w + b
+    if silu:
+        ref = ref / (1 + np.exp(-ref))
+    assert np.max(np.abs(got - ref)) < 2e-5 * max(1.0, np.abs(ref).max())
+
+
+def test_layernorm_known_answer(oracle):
+    # constant row -> 0 (variance 0, eps keeps it finite); [1, 3] -> [-1, 1] * 1/sqrt(1 + eps)
+    x = np.array([[2, 2, 2, 2], [1, 3, 1, 3]], np.float32)
+    got = oracle.layernorm(x, eps=1e-6)
+    assert np.all(got[0] == 0)
+    assert np.allclose(got[1], np.array([-1, 1, -1, 1]) / np.sqrt(1 + 1e-6), atol=1e-7)

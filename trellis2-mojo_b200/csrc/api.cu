@@ -472,6 +472,22 @@ int t2sc_subdivide_device(t2sc_ctx *ctx, const int32_t *coords, int64_t n, const
   });
 }
 
+int t2sc_layernorm_device(t2sc_ctx *ctx, const void *x, void *y, int64_t rows, int c, const float *w,
+                          const float *b, float eps, int flags, int dtype) {
+  if (!ctx) return T2SC_ERR_INVALID;
+  if (rows < 0 || c < 1 || c > 1024) return fail(ctx, T2SC_ERR_INVALID, "layernorm: need rows >= 0, 1 <= c <= 1024");
+  if (rows > 0 && (!x || !y)) return fail(ctx, T2SC_ERR_INVALID, "layernorm: null feature buffer");
+  if ((w == nullptr) != (b == nullptr)) return fail(ctx, T2SC_ERR_INVALID, "layernorm: w and b must both be set or both NULL");
+  if (!(eps >= 0.f)) return fail(ctx, T2SC_ERR_INVALID, "layernorm: eps must be >= 0");
+  if (flags & ~T2SC_SILU) return fail(ctx, T2SC_ERR_INVALID, "layernorm: only T2SC_SILU is a valid flag");
+  if (dtype != T2SC_DT_F32 && dtype != T2SC_DT_F16 && dtype != T2SC_DT_BF16)
+    return fail(ctx, T2SC_ERR_INVALID, "layernorm: unknown dtype");
+  return guarded(ctx, [&]() -> int {
+    DeviceGuard g(ctx->device);
+    return layernorm_device(ctx, x, y, rows, c, w, b, eps, flags, dtype, ctx->last_error);
+  });
+}
+
 int t2sc_subdivide(t2sc_ctx *ctx, const int32_t *coords, int64_t n, const float *sub, int keep_mode,
                    const float *feats, int c, int feats_mode, int32_t *out_coords, float *out_feats,
                    int64_t *out_parent, int64_t *out_subidx, int64_t *m) {

@@ -121,6 +121,10 @@ int subdivide_device(t2sc_ctx *ctx, const int32_t *coords, int64_t n, const floa
                      void *out_feats, int32_t *out_parent, int32_t *out_subidx, int64_t *m,
                      std::string &err);
 
+// ---- LayerNorm (+ SiLU) (norm.cu) ----
+int layernorm_device(t2sc_ctx *ctx, const void *x, void *y, int64_t rows, int c, const float *w, const float *b,
+                     float eps, int flags, int dtype, std::string &err);
+
 // ---- error-flag helpers (api.cu) ----
 int read_dev_err(t2sc_ctx *ctx, int *flags);
 

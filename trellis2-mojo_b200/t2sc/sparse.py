@@ -7,6 +7,7 @@ Same names, argument meaning and error behaviour as the reference:
   SparseUpsample               trellis2_mojo/sparse/spatial/basic.mojo:121-174
   SparseChannel2Spatial        trellis2_mojo/sparse/spatial/spatial2channel.mojo:80-145
   binarize                     trellis2_mojo/models/sc_vaes/sparse_unet_vae.mojo:30-37
+  LayerNorm32                  trellis2_mojo/modules/nn.mojo:297-375 (+ fused SiLU, nn.mojo:614-621)
 
 Every operator runs on the GPU through the C ABI; there is no CPU path.
 Features are host numpy f32 arrays (the reference's Tensor[F32]); the
@@ -305,3 +306,61 @@ class SparseChannel2Spatial:
         """Children where sub != 0, feats = channel slice c*C:(c+1)*C
         (spatial2channel.mojo:97-145)."""
         return _subdivide(x, subdivision, _lib.FEATS_C2S, _lib.SUB_NONZERO)
+
+
+class LayerNorm32:
+    """LayerNorm over the channel dim, statistics in f32 (nn.mojo:297-375),
+    optionally followed by SiLU (the decoder's norm -> activation(ACT_SILU)
+    pairs, sparse_unet_vae.mojo:118,123) in the same kernel."""
+
+    def __init__(self, num_channels, eps=1e-5, affine=True, ctx=None):
+        if num_channels < 1 or num_channels > 1024:
+            raise ValueError("LayerNorm32: 1 <= num_channels <= 1024")
+        self.num_channels, self.eps, self.affine = num_channels, float(eps), affine
+        self.weight = np.ones(num_channels, np.float32) if affine else None   # nn.mojo:311-312
+        self.bias = np.zeros(num_channels, np.float32) if affine else None
+        self.ctx = ctx or Context.default()
+        self._dev_wb = None
+
+    def load(self, weight, bias):
+        self.weight = np.ascontiguousarray(weight, np.float32).reshape(self.num_channels)
+        self.bias = np.ascontiguousarray(bias, np.float32).reshape(self.num_channels)
+        self._dev_wb = None
+
+    def _wb(self):
+        import torch
+        if not self.affine:
+            return None, None
+        if self._dev_wb is None:
+            dev = f"cuda:{self.ctx.device}"
+            self._dev_wb = (torch.from_numpy(self.weight).to(dev), torch.from_numpy(self.bias).to(dev))
+        return self._dev_wb
+
+    def forward_device(self, x, y=None, silu=False):
+        """x: CUDA tensor [rows, C] (float32/float16/bfloat16); y defaults to
+        a new tensor (y may be x). Runs on the context's stream, which is
+        ordered after torch's current stream at entry and before it on return."""
+        import torch
+        dt = {torch.float32: _lib.DT_F32, torch.float16: _lib.DT_F16, torch.bfloat16: _lib.DT_BF16}[x.dtype]
+        if x.dim() != 2 or x.shape[1] != self.num_channels or not x.is_contiguous():
+            raise ValueError("LayerNorm32: x must be contiguous [rows, num_channels]")
+        y = torch.empty_like(x) if y is None else y
+        w, b = self._wb()
+        torch.cuda.current_stream(x.device).synchronize()
+        check(lib.t2sc_layernorm_device(self.ctx.handle, ctypes.c_void_p(x.data_ptr()),
+                                        ctypes.c_void_p(y.data_ptr()), x.shape[0], self.num_channels,
+                                        ctypes.c_void_p(w.data_ptr()) if w is not None else None,
+                                        ctypes.c_void_p(b.data_ptr()) if b is not None else None,
+                                        self.eps, _lib.SILU if silu else 0, dt), self.ctx.handle)
+        self.ctx.synchronize()
+        return y
+
+    def forward(self, feats, silu=False):
+        """feats: host f32 [N, C] or a SparseTensor (then returns x.replace)."""
+        import torch
+        st = feats if isinstance(feats, SparseTensor) else None
+        f = np.ascontiguousarray(st.feats if st is not None else feats, np.float32)
+        y = self.forward_device(torch.from_numpy(f).to(f"cuda:{self.ctx.device}"), silu=silu).cpu().numpy()
+        return st.replace(y) if st is not None else y
+
+    __call__ = forward
