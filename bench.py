@@ -183,7 +183,11 @@ def main():
     ap.add_argument("--overlap", action="store_true",
                     help="N>1: convolve interior rows while the halo is in flight (measured slower at N=4 and 8: "
                          "the second launch per layer costs more than the hidden exchange)")
+    ap.add_argument("--op", default="conv", choices=["conv", "layernorm"],
+                    help="layernorm: time the LayerNorm+SiLU glue kernel alone (not the headline metric)")
     args = ap.parse_args()
+    if args.op == "layernorm":
+        return run_layernorm(args)
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
@@ -191,6 +195,54 @@ def main():
     if args.gpus > 1 or int(os.environ.get("WORLD_SIZE", "1")) > 1:
         return run_distributed(args)
     return run_single(args)
+
+
+def run_layernorm(args, rows=8_000_000, c=64):
+    """LayerNorm(eps 1e-6, affine) + SiLU over bf16 [rows, 64] features in
+    place of the decoder's norm -> activation pairs; 1 GB in and out (larger
+    than L2), so no flush is needed. Algorithmic bytes per launch:
+    2 * rows * c * 2 (+ 512 B of weights)."""
+    import torch
+
+    import t2sc
+    from t2sc import _lib
+    ctx = t2sc.Context.default(0)
+    stream = torch.cuda.Stream()
+    ctx.set_stream(stream.cuda_stream)
+    g = torch.Generator(device="cuda:0").manual_seed(0)
+    x = torch.randn(rows, c, device="cuda:0", generator=g).to(torch.bfloat16)
+    y = torch.empty_like(x)
+    w = torch.randn(c, device="cuda:0", generator=g)
+    b = torch.randn(c, device="cuda:0", generator=g)
+    torch.cuda.synchronize()
+
+    def launch():
+        _lib.check(_lib.lib.t2sc_layernorm_device(ctx.handle, ctypes.c_void_p(x.data_ptr()),
+                                                  ctypes.c_void_p(y.data_ptr()), rows, c,
+                                                  ctypes.c_void_p(w.data_ptr()), ctypes.c_void_p(b.data_ptr()),
+                                                  1e-6, _lib.SILU, _lib.DT_BF16), ctx.handle)
+
+    with torch.cuda.stream(stream):
+        for _ in range(max(args.warmup, 3)):
+            launch()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        stream.synchronize()
+        e0.record(stream)
+        for _ in range(args.steps):
+            launch()
+        e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    alg = 2 * rows * c * 2 + 2 * c * 4
+    _, hbm, src = peaks()
+    gbs = alg / (ms * 1e-3) / 1e9
+    print(json.dumps({"metric": "LayerNorm+SiLU bandwidth, bf16 [8M, 64]", "value": round(gbs, 1), "unit": "GB/s",
+                      "n_gpus": 1, "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": round(ms, 4),
+                      "higher_is_better": True, "dtype": "bf16", "data": "synthetic",
+                      "config": {"workload": f"layernorm_vec_kernel, rows={rows}, C={c}, eps=1e-6, affine, SiLU",
+                                 "l2": "inputs larger than L2"},
+                      "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": hbm, "peak_source": src,
+                                   "unit": "GB/s", "frac": round(gbs / hbm, 3)}}))
 
 
 def run_single(args):

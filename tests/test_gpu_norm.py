@@ -26,11 +26,11 @@ def test_layernorm_f32(t2sc, oracle, c, affine, silu, eps):
     assert np.max(np.abs(got - ref)) < F32_ATOL * max(1.0, np.abs(ref).max())
 
 
-@pytest.mark.parametrize("dtype", ["bfloat16", "float16"])
-def test_layernorm_16bit_inplace(t2sc, oracle, dtype):
+@pytest.mark.parametrize("dtype,c", [("bfloat16", 64), ("float16", 64), ("bfloat16", 12), ("float16", 520)])
+def test_layernorm_16bit_inplace(t2sc, oracle, dtype, c):
+    """C = 64 / 520: 16-byte vector kernel; C = 12 (24-byte rows): scalar kernel."""
     import torch
     S = t2sc.synth
-    c = 64
     x = S.normal(21, (100003, c))
     ln = t2sc.LayerNorm32(c, eps=1e-6, affine=True)
     ln.load(S.normal(22, (c,)), S.normal(23, (c,)))
@@ -50,6 +50,15 @@ def test_layernorm_edges(t2sc, oracle):
     # constant rows normalise to exactly 0
     got = ln.forward(np.full((5, 16), 3.25, np.float32))
     assert np.all(got == 0)
+    # a view 4 bytes off 16-byte alignment takes the scalar kernel
+    x = np.random.default_rng(0).standard_normal((301, 17)).astype(np.float32)
+    xt = torch.from_numpy(x).to("cuda:0")
+    ln16 = t2sc.LayerNorm32(16, eps=1e-6, affine=False)
+    view = xt.view(-1)[1:1 + 300 * 16].view(300, 16)
+    out = torch.empty(300 * 16 + 1, device="cuda:0")[1:].view(300, 16)
+    ln16.forward_device(view, y=out)
+    ref = oracle.layernorm(view.cpu().numpy(), eps=1e-6)
+    assert np.max(np.abs(out.cpu().numpy() - ref)) < F32_ATOL * max(1.0, np.abs(ref).max())
     with pytest.raises(t2sc.T2SCError):
         t2sc._lib.check(t2sc.lib.t2sc_layernorm_device(ln.ctx.handle, None, None, 1, 2048, None, None,
                                                        1e-6, 0, 0), ln.ctx.handle)
