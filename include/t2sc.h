@@ -182,6 +182,22 @@ int t2sc_subdivide_noalloc_device(t2sc_ctx *ctx, const int32_t *coords, int64_t 
                                   int32_t *out_coords, void *out_feats, int32_t *out_parent,
                                   int32_t *out_subidx, int64_t *m);
 
+/* ---- linear layers over feature rows ----
+ * Replaces SparseLinear / linear (trellis2_mojo/modules/nn.mojo:27-266,
+ * :268-293): y = x @ W^T + b, the ConvNeXt block's lin1 / lin2 and the
+ * decoder's to_subdiv (models/sc_vaes/sparse_unet_vae.mojo:38-64, :79).
+ * weight f32 [Co, Ci] host, bias f32 [Co] host (nullable); dtype as for
+ * convs. The handle is a t2sc_conv with a 1x1x1 kernel (free it with
+ * t2sc_conv_destroy) and runs on the same tcgen05 / CUDA-core kernels over
+ * an identity row map, built on the first call for a row count and reused
+ * while the count stays the same. x device [rows, Ci], y device [rows, Co]
+ * (must not alias x), flags T2SC_SILU / T2SC_RESIDUAL (residual [rows, Co])
+ * fused into the epilogue, so lin2(silu(lin1(h))) + x is two calls. */
+int t2sc_linear_create(t2sc_ctx *ctx, const float *weight, const float *bias, int co, int ci, int dtype,
+                       t2sc_conv **out);
+int t2sc_linear_forward_device(t2sc_conv *lin, const void *x, void *y, int64_t rows, int flags,
+                               const void *residual);
+
 /* ---- LayerNorm (+ SiLU) over the channel dim of device features ----
  * Replaces LayerNorm32.forward (trellis2_mojo/modules/nn.mojo:313-370) and,
  * with flags & T2SC_SILU, the activation(..., ACT_SILU) that follows it in

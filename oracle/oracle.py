@@ -49,6 +49,8 @@ def lib():
         L.orc_add.argtypes = [P, P, I64]
         L.orc_round16.restype = None
         L.orc_round16.argtypes = [P, I64, I]
+        L.orc_linear.restype = None
+        L.orc_linear.argtypes = [P, I64, I, P, P, I, I, P, P]
         L.orc_layernorm.restype = None
         L.orc_layernorm.argtypes = [P, I64, I, P, P, ctypes.c_float, I, P]
         L.orc_subdivide.restype = I64
@@ -154,4 +156,15 @@ def layernorm(x, w=None, b=None, eps=1e-6, silu=False):
     w = None if w is None else np.ascontiguousarray(w, np.float32)
     b = None if b is None else np.ascontiguousarray(b, np.float32)
     lib().orc_layernorm(_p(x), x.shape[0], x.shape[1], _p(w), _p(b), eps, int(silu), _p(out))
+    return out
+
+
+def linear(x, w, b=None, silu=False, residual=None):
+    x = np.ascontiguousarray(x, np.float32)
+    w = np.ascontiguousarray(w, np.float32)
+    co, ci = w.shape
+    out = np.empty((x.shape[0], co), np.float32)
+    b = None if b is None else np.ascontiguousarray(b, np.float32)
+    res = None if residual is None else np.ascontiguousarray(residual, np.float32)
+    lib().orc_linear(_p(x), x.shape[0], ci, _p(w), _p(b), co, int(silu), _p(res), _p(out))
     return out

@@ -339,3 +339,16 @@ void orc_layernorm(const float *x, int64_t rows, int c, const float *w, const fl
     }
   }
 }
+
+void orc_linear(const float *x, int64_t rows, int ci, const float *w, const float *b, int co, int silu,
+                const float *res, float *out) {
+  for (int64_t r = 0; r < rows; r++)
+    for (int o = 0; o < co; o++) {
+      float acc = 0.0f;
+      for (int k = 0; k < ci; k++) acc += x[r * ci + k] * w[(int64_t)o * ci + k];
+      if (b) acc += b[o];
+      if (silu) acc = acc / (1.0f + expf(-acc));
+      if (res) acc += res[r * co + o];
+      out[r * co + o] = acc;
+    }
+}

@@ -57,6 +57,13 @@ void orc_add(float *a, const float *b, int64_t n);
 /* Round every value to bf16 (mode 2) or f16 (mode 1), round-to-nearest-even. */
 void orc_round16(float *v, int64_t n, int mode);
 
+/* y = x @ W^T (+ b) (linear, trellis2_mojo/modules/nn.mojo:27-266): each
+ * output a plain sequential f32 sum over k (the packed-GEMM order the
+ * reference documents at nn.mojo:38-44), then optional SiLU and residual
+ * (the epilogue order of the conv). w [co, ci], b nullable, res nullable. */
+void orc_linear(const float *x, int64_t rows, int ci, const float *w, const float *b, int co, int silu,
+                const float *res, float *out);
+
 /* LayerNorm over the last dim (LayerNorm32.forward,
  * trellis2_mojo/modules/nn.mojo:313-370): 8-lane partial sums + halving-tree
  * reduce + scalar tail for the mean and the population variance,

@@ -167,3 +167,17 @@ def test_layernorm_known_answer(oracle):
     got = oracle.layernorm(x, eps=1e-6)
     assert np.all(got[0] == 0)
     assert np.allclose(got[1], np.array([-1, 1, -1, 1]) / np.sqrt(1 + 1e-6), atol=1e-7)
+
+
+def test_linear_oracle(oracle):
+    """orc_linear (nn.mojo:27-266) against the float64 definition, with SiLU and residual."""
+    rng = np.random.default_rng(5)
+    x = rng.standard_normal((131, 24)).astype(np.float32)
+    w = rng.standard_normal((40, 24)).astype(np.float32)
+    b = rng.standard_normal(40).astype(np.float32)
+    res = rng.standard_normal((131, 40)).astype(np.float32)
+    z = x.astype(np.float64) @ w.T.astype(np.float64) + b
+    ref = z / (1 + np.exp(-z)) + res
+    got = oracle.linear(x, w, b, silu=True, residual=res)
+    assert np.max(np.abs(got - ref)) < 1e-4
+    assert np.max(np.abs(oracle.linear(x, w) - x.astype(np.float64) @ w.T.astype(np.float64))) < 1e-4

@@ -329,6 +329,7 @@ int t2sc_conv_destroy(t2sc_conv *cv) {
   cudaFree(cv->d_wtc);
   cudaFree(cv->d_w_simt);
   cudaFree(cv->d_w_lo);
+  free_map(cv->lin_map);
   delete cv;
   return T2SC_OK;
 }
@@ -344,6 +345,36 @@ static int forward_device_impl(t2sc_conv *cv, t2sc_coords *c, const void *x, voi
   T2SC_TRY(build_map(c, cv->kd, cv->kh, cv->kw, cv->dilation, &m, ctx->last_error));
   return cv->tc_path ? conv_tc_launch(cv, m, x, y, flags, residual, ctx->last_error)
                      : conv_simt_launch(cv, m, x, y, flags, residual, ctx->last_error);
+}
+
+int t2sc_linear_create(t2sc_ctx *ctx, const float *weight, const float *bias, int co, int ci, int dtype,
+                       t2sc_conv **out) {
+  // [Co, Ci] is the [Co, 1, 1, 1, Ci] conv weight
+  return t2sc_conv_create(ctx, weight, bias, co, 1, 1, 1, ci, 1, dtype, out);
+}
+
+int t2sc_linear_forward_device(t2sc_conv *lin, const void *x, void *y, int64_t rows, int flags,
+                               const void *residual) {
+  if (!lin) return T2SC_ERR_INVALID;
+  t2sc_ctx *ctx = lin->ctx;
+  if (lin->kvol != 1) return fail(ctx, T2SC_ERR_INVALID, "linear: handle is not a linear layer (kernel volume != 1)");
+  if (rows < 0 || rows > INT32_MAX) return fail(ctx, T2SC_ERR_INVALID, "linear: rows must be in [0, 2^31)");
+  if (flags & ~(T2SC_SILU | T2SC_RESIDUAL)) return fail(ctx, T2SC_ERR_INVALID, "unknown flags");
+  if ((flags & T2SC_RESIDUAL) && !residual) return fail(ctx, T2SC_ERR_INVALID, "RESIDUAL flag without residual");
+  if (rows > 0 && (!x || !y)) return fail(ctx, T2SC_ERR_INVALID, "null feature buffer");
+  if (rows > 0 && x == y) return fail(ctx, T2SC_ERR_INVALID, "linear: y must not alias x");
+  if (rows == 0) return T2SC_OK;
+  return guarded(ctx, [&]() -> int {
+    DeviceGuard g(ctx->device);
+    if (!lin->lin_map || lin->lin_map->n != rows) {
+      cudaStreamSynchronize(ctx->stream);  // the old map may still be read by a launch in flight
+      free_map(lin->lin_map);
+      lin->lin_map = nullptr;
+      T2SC_TRY(build_identity_map(ctx, rows, &lin->lin_map, ctx->last_error));
+    }
+    return lin->tc_path ? conv_tc_launch(lin, lin->lin_map, x, y, flags, residual, ctx->last_error)
+                        : conv_simt_launch(lin, lin->lin_map, x, y, flags, residual, ctx->last_error);
+  });
 }
 
 int t2sc_conv_forward_device(t2sc_conv *cv, t2sc_coords *c, const void *x, void *y, int flags,

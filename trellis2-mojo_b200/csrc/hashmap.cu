@@ -210,6 +210,40 @@ void free_map(t2sc_map *m) {
   delete m;
 }
 
+__global__ void identity_map_kernel(int64_t n, int64_t n_pad, int32_t *__restrict__ nbr, uint32_t *__restrict__ mask,
+                                    int32_t *__restrict__ perm, int32_t *__restrict__ nbr_sorted,
+                                    uint32_t *__restrict__ tile_mask) {
+  const int64_t p = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (p >= n_pad) return;
+  const int32_t r = p < n ? (int32_t)p : -1;
+  perm[p] = r;
+  nbr_sorted[p] = r;
+  if (p < n) nbr[p] = r, mask[p] = 1u;
+  if (p % kTileRows == 0) tile_mask[p / kTileRows] = 1u;  // every tile holds >= 1 row
+}
+
+int build_identity_map(t2sc_ctx *ctx, int64_t n, t2sc_map **out, std::string &err) {
+  std::unique_ptr<t2sc_map, void (*)(t2sc_map *)> m(new t2sc_map(), free_map);
+  m->kvol = 1;
+  m->n = m->n_src = m->n_edges = n;
+  m->ntiles = (n + kTileRows - 1) / kTileRows;
+  m->n_pad = m->ntiles * kTileRows;
+  const size_t np = (size_t)(m->n_pad > 0 ? m->n_pad : 1), nn = (size_t)(n > 0 ? n : 1);
+  T2SC_CUDA(cudaMalloc((void **)&m->nbr, sizeof(int32_t) * nn), "identity map");
+  T2SC_CUDA(cudaMalloc((void **)&m->mask, sizeof(uint32_t) * nn), "identity map");
+  T2SC_CUDA(cudaMalloc((void **)&m->perm, sizeof(int32_t) * np), "identity map");
+  T2SC_CUDA(cudaMalloc((void **)&m->nbr_sorted, sizeof(int32_t) * np), "identity map");
+  T2SC_CUDA(cudaMalloc((void **)&m->tile_mask, sizeof(uint32_t) * (size_t)(m->ntiles > 0 ? m->ntiles : 1)),
+            "identity map");
+  if (n > 0) {
+    identity_map_kernel<<<nblk(m->n_pad, 256), 256, 0, ctx->stream>>>(n, m->n_pad, m->nbr, m->mask, m->perm,
+                                                                      m->nbr_sorted, m->tile_mask);
+    T2SC_LAUNCHED(ctx, "identity_map");
+  }
+  *out = m.release();
+  return T2SC_OK;
+}
+
 int build_map(t2sc_coords *c, int kd, int kh, int kw, int dil, t2sc_map **out, std::string &err) {
   auto key = std::make_tuple(kd, kh, kw, dil);
   auto it = c->maps.find(key);

@@ -81,6 +81,7 @@ struct t2sc_conv {
   int tc_path = 0;               // 1 = tcgen05 path, 0 = SIMT path
   float *d_w_simt = nullptr;     // [K][ci][co] f32 (SIMT path)
   void *d_w_lo = nullptr;        // split-TF32 low parts image (f32 mode)
+  t2sc_map *lin_map = nullptr;   // identity map of the last row count (linear layers)
 };
 
 namespace t2sc {
@@ -88,6 +89,9 @@ namespace t2sc {
 int build_hash(t2sc_coords *c, std::string &err);
 int build_map(t2sc_coords *c, int kd, int kh, int kw, int dil, t2sc_map **out, std::string &err);
 void free_map(t2sc_map *m);
+// One-offset map with nbr[0][r] = r for rows [0, n): a linear layer run
+// through the conv kernels (dense rows, no coordinates).
+int build_identity_map(t2sc_ctx *ctx, int64_t n, t2sc_map **out, std::string &err);
 int export_edges(t2sc_coords *c, t2sc_map *m, int64_t *src, int64_t *tgt, int64_t *kidx, std::string &err);
 int export_csr(t2sc_coords *c, t2sc_map *m, int64_t *row_start, int64_t *src_s, int64_t *kidx_s,
                std::string &err);

@@ -50,6 +50,8 @@ SIGNATURES = {
     "t2sc_subdivide": (I32, [P, P, I64, P, I32, P, I32, I32, P, P, P, P, PI64]),
     "t2sc_subdivide_device": (I32, [P, P, I64, P, I32, P, I32, I32, I32, P, P, P, P, PI64]),
     "t2sc_subdivide_noalloc_device": (I32, [P, P, I64, P, I32, P, I32, I32, I32, P, P, P, P, PI64]),
+    "t2sc_linear_create": (I32, [P, P, P, I32, I32, I32, PP]),
+    "t2sc_linear_forward_device": (I32, [P, P, P, I64, I32, P]),
     "t2sc_layernorm_device": (I32, [P, P, P, I64, I32, P, P, F, I32, I32]),
     "t2sc_synth_shell": (I32, [I32, D, D, U64, I32, P, I64, PI64]),
     "t2sc_synth_normal": (I32, [U64, F, P, I64]),

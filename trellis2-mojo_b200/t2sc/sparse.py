@@ -8,6 +8,7 @@ Same names, argument meaning and error behaviour as the reference:
   SparseChannel2Spatial        trellis2_mojo/sparse/spatial/spatial2channel.mojo:80-145
   binarize                     trellis2_mojo/models/sc_vaes/sparse_unet_vae.mojo:30-37
   LayerNorm32                  trellis2_mojo/modules/nn.mojo:297-375 (+ fused SiLU, nn.mojo:614-621)
+  SparseLinear                 trellis2_mojo/modules/nn.mojo:268-293 (linear, nn.mojo:27-266)
 
 Every operator runs on the GPU through the C ABI; there is no CPU path.
 Features are host numpy f32 arrays (the reference's Tensor[F32]); the
@@ -364,3 +365,79 @@ class LayerNorm32:
         return st.replace(y) if st is not None else y
 
     __call__ = forward
+
+
+def _torch_dtype_code(t):
+    import torch
+    return {torch.float32: _lib.DT_F32, torch.float16: _lib.DT_F16, torch.bfloat16: _lib.DT_BF16}[t]
+
+
+class SparseLinear:
+    """y = x @ weight.T + bias over the channel dim (nn.mojo:268-293), on the
+    conv kernels with a 1x1x1 kernel over an identity row map. weight
+    [Co, Ci], bias [Co]. dtype as SparseConv3d ("f32" f32-accurate, "f16" /
+    "bf16" 16-bit inputs, f32 accumulation). SiLU and a residual add fuse
+    into the epilogue (the ConvNeXt block's lin1/SiLU and lin2 + x)."""
+
+    def __init__(self, weight, bias=None, has_bias=True, dtype="f32", ctx=None):
+        weight = np.ascontiguousarray(weight, dtype=np.float32)
+        if weight.ndim != 2:
+            raise ValueError("SparseLinear: weight must be [Co, Ci]")
+        self.out_features, self.in_features = weight.shape
+        self.has_bias = has_bias and bias is not None
+        self.weight = weight
+        self.bias = np.ascontiguousarray(bias, dtype=np.float32) if self.has_bias else None
+        self.dtype = dtype
+        self.ctx = ctx or Context.default()
+        h = ctypes.c_void_p()
+        check(lib.t2sc_linear_create(self.ctx.handle, _p(weight), _p(self.bias), self.out_features,
+                                     self.in_features, _DTYPES[dtype], ctypes.byref(h)), self.ctx.handle)
+        self.handle = h
+
+    def forward_device(self, x, silu=False, residual=None):
+        """x: CUDA tensor [rows, Ci] of the layer's dtype (float32 for "f32");
+        returns a new [rows, Co] tensor. Runs on the context's stream, ordered
+        after torch's current stream at entry and before it on return."""
+        import torch
+        if x.dim() != 2 or x.shape[1] != self.in_features or not x.is_contiguous():
+            raise ValueError("SparseLinear: x must be contiguous [rows, in_features]")
+        if _torch_dtype_code(x.dtype) != _DTYPES[self.dtype]:
+            raise ValueError("SparseLinear: x dtype does not match the layer's dtype")
+        y = torch.empty((x.shape[0], self.out_features), dtype=x.dtype, device=x.device)
+        flags = (_lib.SILU if silu else 0) | (_lib.RESIDUAL if residual is not None else 0)
+        if residual is not None and (residual.shape != y.shape or residual.dtype != y.dtype
+                                     or not residual.is_contiguous()):
+            raise ValueError("SparseLinear: residual must be a contiguous [rows, out_features] tensor of x's dtype")
+        torch.cuda.current_stream(x.device).synchronize()
+        check(lib.t2sc_linear_forward_device(self.handle, ctypes.c_void_p(x.data_ptr()), ctypes.c_void_p(y.data_ptr()),
+                                             x.shape[0], flags,
+                                             ctypes.c_void_p(residual.data_ptr()) if residual is not None else None),
+              self.ctx.handle)
+        self.ctx.synchronize()
+        return y
+
+    def forward(self, x, silu=False, residual=None):
+        """x: host f32 [N, Ci] or a SparseTensor (then returns x.replace);
+        residual: host f32 [N, Co] / SparseTensor or None."""
+        import torch
+        st = x if isinstance(x, SparseTensor) else None
+        f = np.ascontiguousarray(st.feats if st is not None else x, np.float32)
+        if f.ndim != 2 or f.shape[1] != self.in_features:
+            raise ValueError("SparseLinear: in_features mismatch")
+        tdt = {"f32": torch.float32, "f16": torch.float16, "bf16": torch.bfloat16}[self.dtype]
+        dev = f"cuda:{self.ctx.device}"
+        res = None
+        if residual is not None:
+            r = residual.feats if isinstance(residual, SparseTensor) else residual
+            res = torch.from_numpy(np.ascontiguousarray(r, np.float32)).to(dev, tdt)
+        y = self.forward_device(torch.from_numpy(f).to(dev, tdt), silu=silu, residual=res)
+        y = y.float().cpu().numpy()
+        return st.replace(y) if st is not None else y
+
+    __call__ = forward
+
+    def __del__(self):
+        h = getattr(self, "handle", None)
+        if h and self.ctx.handle:
+            lib.t2sc_conv_destroy(h)
+            self.handle = None
