@@ -113,3 +113,22 @@ def test_host_mirror_argument_errors(t2sc):
         t2sc.SparseTensor(np.zeros((3, 4)), np.zeros((2, 4)))
     with pytest.raises(ValueError):
         t2sc.SparseConv3d(np.zeros((4, 3, 3, 4)), np.zeros(4))  # weight must be 5-D
+
+
+def test_glue_entry_points_reject_null_handles(t2sc):
+    """LayerNorm and linear entry points validate before touching a device."""
+    L = t2sc.lib
+    assert L.t2sc_layernorm_device(None, None, None, 4, 64, None, None, 1e-6, 0, 0) == t2sc._lib.ERR_INVALID
+    assert L.t2sc_linear_forward_device(None, None, None, 4, 0, None) == t2sc._lib.ERR_INVALID
+    out = ctypes.c_void_p()
+    assert L.t2sc_linear_create(None, None, None, 8, 8, 0, ctypes.byref(out)) == t2sc._lib.ERR_INVALID
+
+
+def test_glue_mirror_argument_errors(t2sc):
+    import pytest
+    with pytest.raises(ValueError):
+        t2sc.SparseLinear(np.zeros((4, 3, 2)))        # weight must be [Co, Ci]
+    with pytest.raises(ValueError):
+        t2sc.LayerNorm32(0)
+    with pytest.raises(ValueError):
+        t2sc.LayerNorm32(2048)                        # C <= 1024
