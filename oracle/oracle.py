@@ -59,6 +59,12 @@ def lib():
         L.orc_select_rows.argtypes = [P, I, P, I64, P]
         L.orc_c2s_unfold.restype = None
         L.orc_c2s_unfold.argtypes = [P, I, P, P, I64, P]
+        L.orc_synth_shell.restype = I64
+        L.orc_synth_shell.argtypes = [I, ctypes.c_double, ctypes.c_double, ctypes.c_uint64, I, P, I64]
+        L.orc_synth_normal.restype = None
+        L.orc_synth_normal.argtypes = [ctypes.c_uint64, ctypes.c_float, P, I64]
+        L.orc_synth_bernoulli.restype = None
+        L.orc_synth_bernoulli.argtypes = [ctypes.c_uint64, ctypes.c_double, P, I64]
         _lib = L
     return _lib
 
@@ -167,4 +173,34 @@ def linear(x, w, b=None, silu=False, residual=None):
     b = None if b is None else np.ascontiguousarray(b, np.float32)
     res = None if residual is None else np.ascontiguousarray(residual, np.float32)
     lib().orc_linear(_p(x), x.shape[0], ci, _p(w), _p(b), co, int(silu), _p(res), _p(out))
+    return out
+
+
+# Seeded inputs of the benchmark configurations, generated here so that the
+# CPU reference never loads the product library. name -> (grid, radius, h).
+SHELLS = {
+    "cfg1": (64, 24.0, 1.0),
+    "cfg2": (128, 48.0, 1.75),
+    "cfg3_parent": (128, 48.0, 0.9),
+    "cfg4": (512, 200.0, 0.5),
+    "cfg5_parent": (512, 200.0, 0.5),
+}
+
+
+def synth_shell(g, radius, h, seed=0, batch=0):
+    n = lib().orc_synth_shell(g, radius, h, seed, batch, None, 0)
+    out = np.empty((n, 4), np.int32)
+    lib().orc_synth_shell(g, radius, h, seed, batch, _p(out), n)
+    return out
+
+
+def synth_normal(seed, shape, std=1.0):
+    out = np.empty(shape, np.float32)
+    lib().orc_synth_normal(seed, std, _p(out), out.size)
+    return out
+
+
+def synth_bernoulli(seed, shape, p=0.5):
+    out = np.empty(shape, np.float32)
+    lib().orc_synth_bernoulli(seed, p, _p(out), out.size)
     return out

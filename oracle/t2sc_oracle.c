@@ -352,3 +352,68 @@ void orc_linear(const float *x, int64_t rows, int ci, const float *w, const floa
       out[r * co + o] = acc;
     }
 }
+
+/* ---- seeded inputs, restated independently of the product library so
+ * that the timed CPU reference never loads libt2sc. The RNG is the
+ * project's (trellis2_mojo/rng.mojo:17-52): splitmix64 seeding of an
+ * xorshift64* stream, 53-bit uniforms, Box-Muller normals. ---- */
+typedef struct { uint64_t s; } orc_rng;
+static orc_rng rng_seed(uint64_t seed) {
+  uint64_t z = seed + 0x9E3779B97F4A7C15ULL; /* splitmix64 step */
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ULL;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBULL;
+  z ^= z >> 31;
+  orc_rng r = {z ? z : 0x9E3779B97F4A7C15ULL};
+  return r;
+}
+static uint64_t rng_u64(orc_rng *r) { /* xorshift64* */
+  r->s ^= r->s >> 12;
+  r->s ^= r->s << 25;
+  r->s ^= r->s >> 27;
+  return r->s * 0x2545F4914F6CDD1DULL;
+}
+static double rng_f64(orc_rng *r) { return (double)(rng_u64(r) >> 11) / 9007199254740992.0; }
+
+int64_t orc_synth_shell(int g, double radius, double h, uint64_t seed, int batch, int32_t *coords, int64_t cap) {
+  const double two_pi = 6.283185307179586;
+  double phase = 0.0;
+  if (seed) {
+    orc_rng r = rng_seed(seed);
+    phase = two_pi * rng_f64(&r);
+  }
+  const double c = g / 2.0, lo = 0.9 * radius - h - 1.0, hi = 1.1 * radius + h + 1.0;
+  int64_t m = 0;
+  for (int x = 0; x < g; x++)
+    for (int y = 0; y < g; y++)
+      for (int z = 0; z < g; z++) {
+        double dx = x - c, dy = y - c, dz = z - c;
+        double rad = sqrt(dx * dx + dy * dy + dz * dz);
+        if (rad < lo || rad > hi) continue; /* cannot be within h of the surface */
+        double th = rad > 0 ? acos(dz / rad) : 0.0, ph = atan2(dy, dx) + phase;
+        double surf = radius * (1.0 + 0.1 * sin(3.0 * th) * cos(2.0 * ph));
+        if (fabs(rad - surf) > h) continue;
+        if (coords && m < cap) {
+          coords[4 * m] = batch;
+          coords[4 * m + 1] = x;
+          coords[4 * m + 2] = y;
+          coords[4 * m + 3] = z;
+        }
+        m++;
+      }
+  return m;
+}
+
+void orc_synth_normal(uint64_t seed, float std_, float *out, int64_t count) {
+  orc_rng r = rng_seed(seed);
+  for (int64_t i = 0; i < count; i++) {
+    double u1;
+    do u1 = rng_f64(&r); while (u1 == 0.0);
+    double u2 = rng_f64(&r);
+    out[i] = (float)(sqrt(-2.0 * log(u1)) * cos(6.283185307179586 * u2)) * std_;
+  }
+}
+
+void orc_synth_bernoulli(uint64_t seed, double p, float *out, int64_t count) {
+  orc_rng r = rng_seed(seed);
+  for (int64_t i = 0; i < count; i++) out[i] = rng_f64(&r) < p ? 1.0f : 0.0f;
+}

@@ -88,6 +88,12 @@ void orc_select_rows(const float *x, int c, const int64_t *idx, int64_t m,
 void orc_c2s_unfold(const float *x, int cout, const int64_t *idx,
                     const int64_t *subidx, int64_t m, float *out);
 
+/* Seeded inputs (tests and the CPU reference of bench.py): the shell of
+ * the benchmark configurations and the project RNG (rng.mojo:17-52). */
+int64_t orc_synth_shell(int g, double radius, double h, uint64_t seed, int batch, int32_t *coords, int64_t cap);
+void orc_synth_normal(uint64_t seed, float std_, float *out, int64_t count);
+void orc_synth_bernoulli(uint64_t seed, double p, float *out, int64_t count);
+
 #ifdef __cplusplus
 }
 #endif

@@ -37,3 +37,25 @@ def oracle_conv(O, coords, x, w, b, dil=1, silu=False, residual=None, round_mode
     if residual is not None:
         y = y + residual
     return y
+
+
+def oracle_chain(O, n, x, layers, csr, round_mode=None, residual_last=None):
+    """The reference's conv chain on the oracle with every host thread:
+    layers is a list of (w, b, silu); with round_mode the chain input, the
+    weights and every intermediate are rounded to the 16-bit type the GPU
+    chain keeps between layers. residual_last is added after the last layer
+    (the identity residual of a residual block)."""
+    import os
+    nt = os.cpu_count() or 1
+    h = O.round16(x, round_mode) if round_mode else x
+    for i, (w, b, silu) in enumerate(layers):
+        wr = O.round16(w, round_mode) if round_mode else w
+        h = O.conv_rows(h, wr, b, csr, nt)
+        if silu:
+            h = O.silu(h)
+        if i == len(layers) - 1 and residual_last is not None:
+            r = O.round16(residual_last, round_mode) if round_mode else residual_last
+            h = h + r
+        if round_mode and i < len(layers) - 1:
+            h = O.round16(h, round_mode)
+    return h

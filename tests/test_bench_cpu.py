@@ -19,3 +19,13 @@ def test_reference_arm_json_line():
     assert line["impl"] == "reference" and line["value"] > 0 and line["unit"] == "TFLOP/s"
     assert line["cpu_baseline"]["kind"] == "port" and line["cpu_baseline"]["cores"] >= 1
     assert line["e2e"]["h2d_bytes_per_step"] == 0
+
+
+def test_reference_arm_never_loads_the_product_library():
+    """The reference arm generates its inputs and runs the conv through
+    oracle/ only: libt2sc.so must not be mapped into that process."""
+    code = ("import sys, bench; bench.reference_inputs(); "
+            "maps = open('/proc/self/maps').read(); "
+            "sys.exit(1 if 'libt2sc.so' in maps else 0)")
+    out = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=600, cwd=ROOT)
+    assert out.returncode == 0, out.stderr[-2000:]

@@ -50,8 +50,9 @@ def test_linear_row_count_change_and_errors(t2sc, oracle):
     assert lin.forward_device(xt).shape == (0, 32)
     conv = t2sc.SparseConv3d(S.normal(52, (16, 3, 3, 3, 16)), None)
     xt = torch.zeros((4, 16), device="cuda:0")
+    yt = torch.empty((4, 16), device="cuda:0")
     with pytest.raises(t2sc.T2SCError):   # a 3x3x3 conv handle is not a linear layer
-        t2sc._lib.check(t2sc.lib.t2sc_linear_forward_device(conv.handle, xt.data_ptr(), xt.data_ptr() + 4096, 4,
+        t2sc._lib.check(t2sc.lib.t2sc_linear_forward_device(conv.handle, xt.data_ptr(), yt.data_ptr(), 4,
                                                             0, None), conv.ctx.handle)
 
 

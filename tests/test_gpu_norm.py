@@ -81,3 +81,27 @@ def test_decoder_glue_chain(t2sc, oracle):
     h_ref = oracle.layernorm(x, ln.weight, ln.bias, 1e-6, True)
     y_ref = oracle_conv(oracle, coords, h_ref, w, b)
     assert rel_err(y, y_ref) < F32_TOL
+
+
+def test_layernorm_rejects_bad_y(t2sc):
+    import torch
+    ln = t2sc.LayerNorm32(16)
+    x = torch.zeros((4, 16), device="cuda:0")
+    for y in (torch.zeros((3, 16), device="cuda:0"),                      # too small
+              torch.zeros((4, 16), device="cuda:0", dtype=torch.bfloat16),  # wrong dtype
+              torch.zeros((16, 4), device="cuda:0").t(),                  # not contiguous
+              torch.zeros((4, 16))):                                      # host memory
+        with pytest.raises(ValueError):
+            ln.forward_device(x, y=y)
+    with pytest.raises(ValueError):
+        ln.forward_device(torch.zeros((4, 16)))
+
+
+def test_linear_rejects_host_residual(t2sc):
+    import torch
+    lin = t2sc.SparseLinear(np.zeros((16, 16), np.float32))
+    x = torch.zeros((4, 16), device="cuda:0")
+    with pytest.raises(ValueError):
+        lin.forward_device(x, residual=torch.zeros((4, 16)))
+    with pytest.raises(ValueError):
+        lin.forward_device(torch.zeros((4, 16)))

@@ -181,3 +181,15 @@ def test_linear_oracle(oracle):
     got = oracle.linear(x, w, b, silu=True, residual=res)
     assert np.max(np.abs(got - ref)) < 1e-4
     assert np.max(np.abs(oracle.linear(x, w) - x.astype(np.float64) @ w.T.astype(np.float64))) < 1e-4
+
+
+def test_oracle_inputs_match_the_library_generator(oracle, t2sc):
+    """The oracle's own seeded-input generator (used by the CPU reference
+    arm) and the library's give the same shells, normals and masks."""
+    for name in ("cfg1", "cfg2", "cfg3_parent"):
+        for seed in (0, 3):
+            a = oracle.synth_shell(*oracle.SHELLS[name], seed=seed)
+            b = t2sc.synth.shell(*t2sc.synth.SHELLS[name], seed=seed)
+            assert np.array_equal(a, b), (name, seed)
+    assert np.array_equal(oracle.synth_normal(401, (27, 64), 0.1), t2sc.synth.normal(401, (27, 64), std=0.1))
+    assert np.array_equal(oracle.synth_bernoulli(500, (1000, 8)), t2sc.synth.bernoulli(500, (1000, 8)))

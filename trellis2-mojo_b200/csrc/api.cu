@@ -1,5 +1,6 @@
 // C-ABI entry points of libt2sc (declared in include/t2sc.h).
 #include <stdio.h>
+#include <stdlib.h>
 
 #include <new>
 #include <vector>
@@ -115,6 +116,10 @@ int t2sc_ctx_create(int device, t2sc_ctx **out) {
       cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep);
     }
     ctx->stream = ctx->own_stream;
+    // tuning knobs (tile grouping only; results do not depend on them)
+    if (const char *e = getenv("T2SC_TILE_ORDER")) ctx->tile_order = atoi(e);
+    if (const char *e = getenv("T2SC_TILE_CHUNK")) ctx->tile_chunk = atoll(e);
+    if (ctx->tile_order < 0 || ctx->tile_order > 2) ctx->tile_order = 0;
     if (cudaMalloc((void **)&ctx->d_err, sizeof(int)) != cudaSuccess) return T2SC_ERR_OOM;
     if (cudaMemset(ctx->d_err, 0, sizeof(int)) != cudaSuccess) return T2SC_ERR_CUDA;
     *out = ctx.release();
@@ -234,7 +239,9 @@ int t2sc_coords_build_map(t2sc_coords *c, int kd, int kh, int kw, int dil, int64
     DeviceGuard g(ctx->device);
     t2sc_map *m = nullptr;
     T2SC_TRY(build_map(c, kd, kh, kw, dil, &m, ctx->last_error));
-    if (n_edges) *n_edges = m->n_edges;
+    int64_t e = 0;
+    if (n_edges) T2SC_TRY(map_edges(m, &e, ctx->last_error));
+    if (n_edges) *n_edges = e;
     return T2SC_OK;
   });
 }
@@ -248,7 +255,7 @@ int t2sc_neighbor_map_export(t2sc_coords *c, int kd, int kh, int kw, int dil, in
     DeviceGuard g(ctx->device);
     t2sc_map *m = nullptr;
     T2SC_TRY(build_map(c, kd, kh, kw, dil, &m, ctx->last_error));
-    *n_edges = m->n_edges;
+    T2SC_TRY(map_edges(m, n_edges, ctx->last_error));
     if (m->n_edges > cap) return fail(ctx, T2SC_ERR_CAPACITY, "edge buffers too small");
     if (m->n_edges > 0 && (!src || !tgt || !kidx)) return fail(ctx, T2SC_ERR_INVALID, "null edge buffer");
     T2SC_TRY(export_edges(c, m, src, tgt, kidx, ctx->last_error));
@@ -265,7 +272,7 @@ int t2sc_csr_export(t2sc_coords *c, int kd, int kh, int kw, int dil, int64_t *ro
     DeviceGuard g(ctx->device);
     t2sc_map *m = nullptr;
     T2SC_TRY(build_map(c, kd, kh, kw, dil, &m, ctx->last_error));
-    *n_edges = m->n_edges;
+    T2SC_TRY(map_edges(m, n_edges, ctx->last_error));
     if (m->n_edges > cap) return fail(ctx, T2SC_ERR_CAPACITY, "edge buffers too small");
     if (m->n_edges > 0 && (!src_s || !kidx_s)) return fail(ctx, T2SC_ERR_INVALID, "null edge buffer");
     T2SC_TRY(export_csr(c, m, row_start, src_s, kidx_s, ctx->last_error));

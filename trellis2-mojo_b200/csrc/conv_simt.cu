@@ -1,6 +1,7 @@
 // CUDA-core SubM conv used where the tensor-core kernel's shape rules do not
 // hold (Ci % 8 != 0 or Co % 16 != 0) and, in this build, for the f32 mode.
-// Output-stationary like the tensor-core kernel: a block owns 32 rows x 64
+// Output-stationary like the tensor-core kernel: a block owns 32 rows (in
+// the map's sorted order, written back to their own positions) x 64
 // output channels, stages each offset's 32 neighbour rows and the matching
 // weight slice in shared memory, and accumulates with FMAs in f32 (k
 // ascending, then input channel ascending).
@@ -34,8 +35,9 @@ template <int DT>
 __global__ void __launch_bounds__(256) conv_simt_kernel(const void *__restrict__ x, void *__restrict__ y,
                                                         const void *__restrict__ res, const float *__restrict__ w,
                                                         const float *__restrict__ bias,
-                                                        const int32_t *__restrict__ nbr, int64_t n, int ci, int co,
-                                                        int kvol, int flags) {
+                                                        const int32_t *__restrict__ nbr_sorted,
+                                                        const int32_t *__restrict__ perm, int64_t n_pad, int ci,
+                                                        int co, int kvol, int flags) {
   __shared__ float xs[kRows][kCiChunk + 1];
   __shared__ float ws[kCiChunk][kCols];
   __shared__ int32_t srcs[kRows];
@@ -48,8 +50,7 @@ __global__ void __launch_bounds__(256) conv_simt_kernel(const void *__restrict__
   for (int k = 0; k < kvol; k++) {
     __syncthreads();
     if (threadIdx.x < kRows) {
-      int64_t r = r0 + threadIdx.x;
-      srcs[threadIdx.x] = r < n ? nbr[(int64_t)k * n + r] : -1;
+      srcs[threadIdx.x] = nbr_sorted[(int64_t)k * n_pad + r0 + threadIdx.x];
     }
     __syncthreads();
     for (int c0 = 0; c0 < ci; c0 += kCiChunk) {
@@ -76,8 +77,8 @@ __global__ void __launch_bounds__(256) conv_simt_kernel(const void *__restrict__
   if (o >= co) return;
 #pragma unroll
   for (int i = 0; i < 8; i++) {
-    const int64_t r = r0 + ty + 4 * i;
-    if (r >= n) continue;
+    const int64_t r = perm[r0 + ty + 4 * i];  // sorted position -> output row
+    if (r < 0) continue;
     float v = acc[i] + bias[o];
     if (flags & T2SC_SILU) v = v / (1.0f + expf(-v));
     if (flags & T2SC_RESIDUAL) v += load_el<DT>(res, r * co + o);
@@ -110,19 +111,23 @@ int conv_simt_prepare(t2sc_conv *cv, const float *w, std::string &err) {
 int conv_simt_launch(t2sc_conv *cv, t2sc_map *m, const void *x, void *y, int flags, const void *residual,
                      std::string &err) {
   if (m->n == 0) return T2SC_OK;
-  dim3 grid((unsigned)((m->n + kRows - 1) / kRows), (unsigned)((cv->co + kCols - 1) / kCols));
+  // rows in the map's sorted order (n_pad is a multiple of the 32-row block)
+  dim3 grid((unsigned)(m->n_pad / kRows), (unsigned)((cv->co + kCols - 1) / kCols));
   cudaStream_t st = cv->ctx->stream;
   switch (cv->dtype) {
     case T2SC_DT_F32:
-      conv_simt_kernel<T2SC_DT_F32><<<grid, 256, 0, st>>>(x, y, residual, cv->d_w_simt, cv->d_bias, m->nbr, m->n,
+      conv_simt_kernel<T2SC_DT_F32><<<grid, 256, 0, st>>>(x, y, residual, cv->d_w_simt, cv->d_bias, m->nbr_sorted, m->perm,
+                                                          m->n_pad,
                                                           cv->ci, cv->co, cv->kvol, flags);
       break;
     case T2SC_DT_BF16:
-      conv_simt_kernel<T2SC_DT_BF16><<<grid, 256, 0, st>>>(x, y, residual, cv->d_w_simt, cv->d_bias, m->nbr, m->n,
+      conv_simt_kernel<T2SC_DT_BF16><<<grid, 256, 0, st>>>(x, y, residual, cv->d_w_simt, cv->d_bias, m->nbr_sorted, m->perm,
+                                                          m->n_pad,
                                                            cv->ci, cv->co, cv->kvol, flags);
       break;
     default:
-      conv_simt_kernel<T2SC_DT_F16><<<grid, 256, 0, st>>>(x, y, residual, cv->d_w_simt, cv->d_bias, m->nbr, m->n,
+      conv_simt_kernel<T2SC_DT_F16><<<grid, 256, 0, st>>>(x, y, residual, cv->d_w_simt, cv->d_bias, m->nbr_sorted, m->perm,
+                                                          m->n_pad,
                                                           cv->ci, cv->co, cv->kvol, flags);
   }
   T2SC_LAUNCHED(cv->ctx, "conv_simt");

@@ -45,6 +45,10 @@
 #include "internal.h"
 #include "sm100.cuh"
 
+#ifndef T2SC_CONV_DIAGNOSTICS
+#define T2SC_CONV_DIAGNOSTICS 0
+#endif
+
 #ifndef T2SC_COPY_WARPS_128
 #define T2SC_COPY_WARPS_128 8
 #endif
@@ -90,15 +94,31 @@ struct TcArgs {
   int ntiles, ci, co, bn, nchunks, nco_tiles, kvol, stages, flags, tmem_cols;
   uint32_t a_bytes, b_bytes, sub_bytes, stage_bytes;  // per (k, chunk) pair: A, B; pair slot; stage
   int group;                                          // (k, chunk) pairs per pipeline stage
-  int debug;  // diagnostics (T2SC_CONV_DEBUG): 2 skips the MMAs, 4 the epilogue stores
-  int *err;
+#if T2SC_CONV_DIAGNOSTICS
+  int debug;  // diagnostics (T2SC_CONV_DEBUG): 1 skips the gathers, 2 the MMAs, 4 the epilogue stores
   long long *trace;  // diagnostics (T2SC_CONV_TRACE): per-stage clocks of CTA 0, or null
+#endif
+  int l1;          // gather through L1 (cp.async.ca) instead of L2 only (.cg)
+  int contiguous;  // CTA b takes units [b*U/G, (b+1)*U/G) instead of b, b+G, b+2G, ...
+  uint32_t backoff_epi, backoff_ctl, backoff_copy;
+  int wait_mode;  // how a waiting thread polls an mbarrier (sm100::mbar_wait_bounded)  // sleep between polls of a waiting warp (ns; 0 = spin)
+  int *err;
 };
+// Diagnostics build only (-DT2SC_CONV_DIAGNOSTICS=1, never the product
+// library): switches that skip parts of the work and a per-stage clock trace.
+#if T2SC_CONV_DIAGNOSTICS
 constexpr int kTraceN = 4096;
 #define T2SC_TRACE(slot, idx)                                                     \
   do {                                                                            \
     if (a.trace && blockIdx.x == 0 && (idx) < kTraceN) a.trace[(slot) * kTraceN + (idx)] = clock64(); \
   } while (0)
+#define T2SC_SKIP(bit) (a.debug & (bit))
+#else
+#define T2SC_TRACE(slot, idx) \
+  do {                        \
+  } while (0)
+#define T2SC_SKIP(bit) false
+#endif
 
 template <int DT>
 __device__ __forceinline__ uint32_t pack2(float a, float b) {
@@ -180,13 +200,43 @@ __device__ __forceinline__ void store16(const TcArgs &a, int orow, int col, cons
   yp[1] = o1;
 }
 
-// Warp-uniform bounded wait: every lane probes the barrier (the common
-// case, an already completed phase, costs one probe); a lane that has to
-// wait falls into the bounded loop; the verdict is agreed with a vote.
-__device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, volatile int *abort, int *err) {
+// Warp-uniform bounded wait. Every lane probes the barrier (the common
+// case, an already completed phase, costs one probe). Otherwise lane 0
+// alone polls, sleeping `backoff_ns` between polls so that a waiting warp
+// leaves the issue slots to the working ones, and the other lanes then
+// observe the completed phase themselves (each consumer lane acquires it).
+__device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, volatile int *abort, int *err,
+                                          uint32_t backoff_ns = 0, int g_wait_mode = 0) {
   bool ok = sm100::mbar_test_wait(bar, parity);
   if (__all_sync(0xffffffffu, ok)) return true;
-  if (!ok) ok = sm100::mbar_wait_bounded(bar, parity, abort, err, kDevErrTimeout, kWaitLimit);
+  if (backoff_ns == 0) {
+    if (!ok) ok = sm100::mbar_wait_bounded(bar, parity, abort, err, kDevErrTimeout, kWaitLimit, g_wait_mode);
+    return __all_sync(0xffffffffu, ok);
+  }
+  int done = 0;
+  if ((threadIdx.x & 31) == 0) {
+    const long long t0 = clock64();
+    for (uint32_t i = 1;; i++) {
+      if (sm100::mbar_test_wait(bar, parity)) {
+        done = 1;
+        break;
+      }
+      __nanosleep(backoff_ns);
+      if ((i & 7) == 0) {
+        if (*abort) break;
+        if (clock64() - t0 > kWaitLimit) {
+          *abort = 1;
+          atomicOr(err, kDevErrTimeout);
+          break;
+        }
+      }
+    }
+  }
+  done = __shfl_sync(0xffffffffu, done, 0);
+  if (!done) return false;
+  ok = sm100::mbar_test_wait(bar, parity);
+  if (__all_sync(0xffffffffu, ok)) return true;
+  if (!ok) ok = sm100::mbar_wait_bounded(bar, parity, abort, err, kDevErrTimeout, kWaitLimit, g_wait_mode);
   return __all_sync(0xffffffffu, ok);
 }
 
@@ -242,6 +292,14 @@ __global__ void __launch_bounds__(Roles<DT, RB>::kThreads, 1)
   sm100::tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const int nunits = a.ntiles * a.nco_tiles;
+  const int ubeg = (int)((int64_t)blockIdx.x * nunits / gridDim.x);
+  const int uend = (int)((int64_t)(blockIdx.x + 1) * nunits / gridDim.x);
+  // unit of this CTA's i-th iteration (nunits past its last one)
+  auto unit_at = [&](int i) -> int {
+    if (a.contiguous) return ubeg + i < uend ? ubeg + i : nunits;
+    const int64_t u = (int64_t)blockIdx.x + (int64_t)i * gridDim.x;
+    return u < nunits ? (int)u : nunits;
+  };
 
   // tile masks are read ahead so no global-load latency sits at a unit boundary
   auto mask_of = [&](int unit) -> uint32_t { return unit < nunits ? __ldg(a.tile_mask + unit / a.nco_tiles) : 0u; };
@@ -266,14 +324,14 @@ __global__ void __launch_bounds__(Roles<DT, RB>::kThreads, 1)
     const uint32_t row_stride = (uint32_t)(a.ci * ES);
     const int64_t lo_delta = kSplit ? (a.x_lo - a.x) : 0;
     const int G = a.group;
-    uint32_t s = 0, ph = 0, t = 0;
+    uint32_t s = 0, ph = 0, t = 0, cit = 0;
     bool ok = true;
-    uint32_t km_next = mask_of(blockIdx.x);
-    for (int u = blockIdx.x; u < nunits && ok; u += gridDim.x, t++) {
+    uint32_t km_next = mask_of(unit_at(0));
+    for (int i = 0, u = unit_at(0); u < nunits && ok; u = unit_at(++i), t++) {
       uint32_t km = km_next;
-      km_next = mask_of(u + gridDim.x);
+      km_next = mask_of(unit_at(i + 1));
       const int npairs = __popc(km) * a.nchunks;
-      if (npairs > 0 && !warp_wait(idxf0 + 8 * (t & 1), (t >> 1) & 1, abort, a.err)) {
+      if (npairs > 0 && !warp_wait(idxf0 + 8 * (t & 1), (t >> 1) & 1, abort, a.err, 0, a.wait_mode)) {
         ok = false;
         break;
       }
@@ -282,10 +340,12 @@ __global__ void __launch_bounds__(Roles<DT, RB>::kThreads, 1)
       const uint8_t *gp[RPL];
       uint32_t gs[RPL];
       for (int q = 0; q < npairs && ok;) {
-        if (!warp_wait(empty0 + 8 * s, ph ^ 1, abort, a.err)) {
+        if (tid == 32 * kCopyWarp0) T2SC_TRACE(0, cit);
+        if (!warp_wait(empty0 + 8 * s, ph ^ 1, abort, a.err, a.backoff_copy, a.wait_mode)) {
           ok = false;
           break;
         }
+        if (tid == 32 * kCopyWarp0) T2SC_TRACE(1, cit);
         const uint32_t abase = sbase + s * a.stage_bytes, bar = full0 + 8 * s;
         const int valid = npairs - q < G ? npairs - q : G;
         for (int g = 0; g < valid; g++, q++) {
@@ -317,7 +377,11 @@ __global__ void __launch_bounds__(Roles<DT, RB>::kThreads, 1)
 #pragma unroll
           for (int p = 0; p < RPL; p++) {
             const uint32_t sz = cvalid ? gs[p] : 0u;
-            if (!(a.debug & 1)) {
+            if (T2SC_SKIP(1)) {
+            } else if (a.l1) {
+              sm100::cp_async_16_ca(sub + soff[p], gp[p] + c * RB, sz);
+              if (kSplit) sm100::cp_async_16_ca(sub + a_tile + soff[p], gp[p] + lo_delta + c * RB, sz);
+            } else {
               sm100::cp_async_16(sub + soff[p], gp[p] + c * RB, sz);
               if (kSplit) sm100::cp_async_16(sub + a_tile + soff[p], gp[p] + lo_delta + c * RB, sz);
             }
@@ -325,6 +389,8 @@ __global__ void __launch_bounds__(Roles<DT, RB>::kThreads, 1)
         }
         // arrives on the stage barrier once this lane's copies have landed
         sm100::cp_async_arrive_noinc(bar);
+        if (tid == 32 * kCopyWarp0) T2SC_TRACE(6, cit);
+        cit++;
         if (++s == (uint32_t)S) {
           s = 0;
           ph ^= 1;
@@ -353,21 +419,24 @@ __global__ void __launch_bounds__(Roles<DT, RB>::kThreads, 1)
     };
     uint32_t it = 0, s = 0, ph = 0, t = 0, n_idx = 0;
     bool ok = true;
-    uint32_t km_cur = mask_of(blockIdx.x), km_n1 = mask_of(blockIdx.x + gridDim.x);
-    load_idx(blockIdx.x, 0, km_cur);  // buffer 0 starts free
-    n_idx = 1;
-    for (int u = blockIdx.x; u < nunits && ok; u += gridDim.x, t++) {
+    uint32_t km_cur = mask_of(unit_at(0)), km_n1 = mask_of(unit_at(1));
+    if (unit_at(0) < nunits) {
+      load_idx(unit_at(0), 0, km_cur);  // buffer 0 starts free
+      n_idx = 1;
+    }
+    for (int i = 0, u = unit_at(0); u < nunits && ok; u = unit_at(++i), t++) {
       const int cot = u % a.nco_tiles;
       const uint32_t km = km_cur;
-      const uint32_t km_n2 = mask_of(u + 2 * gridDim.x);
-      if (u + (int)gridDim.x < nunits) {
+      const uint32_t km_n2 = mask_of(unit_at(i + 2));
+      const int u_next = unit_at(i + 1);
+      if (u_next < nunits) {
         // the other buffer held unit t-1: wait until every copy warp is done with it
         const uint32_t nb = (t + 1) & 1;
-        if (!warp_wait(idxe0 + 8 * nb, (((t + 1) >> 1) & 1) ^ 1, abort, a.err)) {
+        if (!warp_wait(idxe0 + 8 * nb, (((t + 1) >> 1) & 1) ^ 1, abort, a.err, a.backoff_ctl, a.wait_mode)) {
           ok = false;
           break;
         }
-        load_idx(u + gridDim.x, nb, km_n1);
+        load_idx(u_next, nb, km_n1);
         n_idx++;
       }
       km_cur = km_n1;
@@ -378,13 +447,15 @@ __global__ void __launch_bounds__(Roles<DT, RB>::kThreads, 1)
       int c = a.nchunks;
       const uint8_t *wk = a.wimg;
       for (int q = 0; q < npairs && ok;) {
-        if (!warp_wait(empty0 + 8 * s, ph ^ 1, abort, a.err)) {
+        if (lane == 0) T2SC_TRACE(7, it);
+        if (!warp_wait(empty0 + 8 * s, ph ^ 1, abort, a.err, a.backoff_ctl, a.wait_mode)) {
           ok = false;
           break;
         }
         const int valid = npairs - q < a.group ? npairs - q : a.group;
         const uint32_t bar = full0 + 8 * s, abase = sbase + s * a.stage_bytes;
-        if (lane == 0) sm100::mbar_arrive_expect_tx(bar, (uint32_t)valid * a.b_bytes);
+        if (lane == 0) T2SC_TRACE(8, it);
+        if (lane == 0) sm100::mbar_arrive_expect_tx(bar, T2SC_SKIP(8) ? 0u : (uint32_t)valid * a.b_bytes);
         for (int g = 0; g < valid; g++, q++) {
           if (++c >= a.nchunks) {
             c = 0;
@@ -392,7 +463,7 @@ __global__ void __launch_bounds__(Roles<DT, RB>::kThreads, 1)
             m &= m - 1;
             wk = a.wimg + (size_t)((size_t)cot * a.kvol + k) * a.nchunks * a.b_bytes;
           }
-          if (lane == 0)
+          if (lane == 0 && !T2SC_SKIP(8))
             sm100::bulk_g2s(abase + g * a.sub_bytes + a.a_bytes, wk + (size_t)c * a.b_bytes, a.b_bytes, bar);
         }
         it++;
@@ -422,16 +493,19 @@ __global__ void __launch_bounds__(Roles<DT, RB>::kThreads, 1)
     auto orow_of = [&](int unit) -> int {
       return unit < nunits ? __ldg(a.perm + (int64_t)(unit / a.nco_tiles) * kTileRows + row) : -1;
     };
-    uint32_t km_next = mask_of(blockIdx.x);
-    int orow_next = orow_of(blockIdx.x);
-    for (int u = blockIdx.x; u < nunits; u += gridDim.x) {
+    uint32_t km_next = mask_of(unit_at(0));
+    int orow_next = orow_of(unit_at(0));
+    for (int i = 0, u = unit_at(0); u < nunits; u = unit_at(++i)) {
       const int cot = u % a.nco_tiles;
       const uint32_t km = km_next;
       const int orow = orow_next;
-      km_next = mask_of(u + gridDim.x);
-      orow_next = orow_of(u + gridDim.x);
+      km_next = mask_of(unit_at(i + 1));
+      orow_next = orow_of(unit_at(i + 1));
       const int col0 = cot * a.bn;
       if (km == 0) {
+        // no offset of the tile has a source (not reachable for submanifold
+        // maps, whose centre offset always hits): the epilogue of a zero sum,
+        // bias -> SiLU -> residual, still applies
         if (orow >= 0) {
           float z[16];
 #pragma unroll
@@ -447,7 +521,7 @@ __global__ void __launch_bounds__(Roles<DT, RB>::kThreads, 1)
         bool ok = true;
         for (int kk = __popc(km); kk > 0; kk--) {
           const uint32_t b = acc_it & 1;
-          if (!warp_wait(tfull0 + 8 * b, (acc_it >> 1) & 1, abort, a.err)) {
+          if (!warp_wait(tfull0 + 8 * b, (acc_it >> 1) & 1, abort, a.err, a.backoff_epi, a.wait_mode)) {
             ok = false;
             break;
           }
@@ -469,7 +543,7 @@ __global__ void __launch_bounds__(Roles<DT, RB>::kThreads, 1)
           acc_it++;
         }
         if (!ok) break;
-        if (orow >= 0 && !(a.debug & 4)) {
+        if (orow >= 0 && !T2SC_SKIP(4)) {
 #pragma unroll
           for (int cc = 0; cc < kTf32MaxBn; cc += 16) {
             if (cc < a.bn) {
@@ -484,7 +558,7 @@ __global__ void __launch_bounds__(Roles<DT, RB>::kThreads, 1)
       }
       const uint32_t b = acc_it & 1;
       if (tid == 0) T2SC_TRACE(4, acc_it);
-      if (!warp_wait(tfull0 + 8 * b, (acc_it >> 1) & 1, abort, a.err)) break;
+      if (!warp_wait(tfull0 + 8 * b, (acc_it >> 1) & 1, abort, a.err, a.backoff_epi, a.wait_mode)) break;
       if (tid == 0) T2SC_TRACE(5, acc_it);
       sm100::tc_fence_after();
       const uint32_t tbase = tmem + ((uint32_t)(32 * q) << 16) + b * a.bn;
@@ -495,7 +569,7 @@ __global__ void __launch_bounds__(Roles<DT, RB>::kThreads, 1)
         float acc[16];
 #pragma unroll
         for (int i = 0; i < 16; i++) acc[i] = __uint_as_float(r[i]);
-        if (orow >= 0 && !(a.debug & 4)) store16<DT>(a, orow, col0 + cc, acc);
+        if (orow >= 0 && !T2SC_SKIP(4)) store16<DT>(a, orow, col0 + cc, acc);
       }
       sm100::tc_fence_before();
       __syncwarp();
@@ -512,10 +586,10 @@ __global__ void __launch_bounds__(Roles<DT, RB>::kThreads, 1)
       const uint64_t dA = sm100::smem_desc(sbase, RB), dB = sm100::smem_desc(sbase + a.a_bytes, RB);
       uint32_t s = 0, ph = 0, acc_it = 0, mit = 0;
       bool ok = true;
-      uint32_t km_next = mask_of(blockIdx.x);
-      for (int u = blockIdx.x; u < nunits && ok; u += gridDim.x) {
+      uint32_t km_next = mask_of(unit_at(0));
+      for (int i = 0, u = unit_at(0); u < nunits && ok; u = unit_at(++i)) {
         const uint32_t km = km_next;
-        km_next = mask_of(u + gridDim.x);
+        km_next = mask_of(unit_at(i + 1));
         if (km == 0) continue;
         const int nk = __popc(km);
         // split-TF32: one accumulator (and one drain) per offset (G = 1);
@@ -524,7 +598,7 @@ __global__ void __launch_bounds__(Roles<DT, RB>::kThreads, 1)
         for (int gi = 0; gi < groups && ok; gi++) {
           const uint32_t b = acc_it & 1;
           if (!sm100::mbar_wait_bounded(tempty0 + 8 * b, ((acc_it >> 1) & 1) ^ 1, abort, a.err, kDevErrTimeout,
-                                        kWaitLimit)) {
+                                        kWaitLimit, a.wait_mode)) {
             ok = false;
             break;
           }
@@ -533,10 +607,11 @@ __global__ void __launch_bounds__(Roles<DT, RB>::kThreads, 1)
           uint32_t accum = 0;
           for (int q = 0; q < pairs_per_group; q += a.group) {
             T2SC_TRACE(2, mit);
-            if (!sm100::mbar_wait_bounded(full0 + 8 * s, ph, abort, a.err, kDevErrTimeout, kWaitLimit)) {
+            if (!sm100::mbar_wait_bounded(full0 + 8 * s, ph, abort, a.err, kDevErrTimeout, kWaitLimit, a.wait_mode)) {
               ok = false;
               break;
             }
+            T2SC_TRACE(9, mit);
             sm100::tc_fence_after();
             const int valid = pairs_per_group - q < a.group ? pairs_per_group - q : a.group;
             for (int g = 0; g < valid; g++) {
@@ -544,7 +619,7 @@ __global__ void __launch_bounds__(Roles<DT, RB>::kThreads, 1)
 #pragma unroll
               for (int kk = 0; kk < RB / 32; kk++) {
                 const uint64_t ahi = dA + so + kk * 2, bhi = dB + so + kk * 2;
-                if (a.debug & 2) {
+                if (T2SC_SKIP(2)) {
                 } else if (kSplit) {
                   const uint64_t alo = ahi + (a_tile >> 4), blo = bhi + (b_tile >> 4);
                   sm100::mma_tf32(dtm, alo, bhi, idesc, accum);
@@ -613,6 +688,7 @@ int launch_tc(t2sc_conv *cv, const TcArgs &args, int grid, size_t smem, std::str
     T2SC_CUDA(cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem), "tc smem attr");
     if (dev >= 0 && dev < 64) attr_smem[dev] = (int)smem;
   }
+#if T2SC_CONV_DIAGNOSTICS
   const char *trace_path = getenv("T2SC_CONV_TRACE");
   if (trace_path) {  // diagnostics only: allocates, synchronises and writes a file
     TcArgs t = args;
@@ -631,6 +707,7 @@ int launch_tc(t2sc_conv *cv, const TcArgs &args, int grid, size_t smem, std::str
     }
     return T2SC_OK;
   }
+#endif
   kfn<<<grid, Roles<DT, RB>::kThreads, smem, cv->ctx->stream>>>(args);
   T2SC_LAUNCHED(cv->ctx, "conv_tc");
   return T2SC_OK;
@@ -728,12 +805,33 @@ int conv_tc_launch(t2sc_conv *cv, t2sc_map *m, const void *x, void *y, int flags
   a.kvol = cv->kvol;
   a.flags = flags;
   a.err = cv->ctx->d_err;
+#if T2SC_CONV_DIAGNOSTICS
   static const int debug_bits = [] {
     const char *e = getenv("T2SC_CONV_DEBUG");
     return e ? atoi(e) : 0;
   }();
   a.debug = debug_bits;
   a.trace = nullptr;
+#endif
+  static const int l1_env = [] {
+    const char *e = getenv("T2SC_CONV_L1");
+    return e ? atoi(e) : 0;
+  }();
+  static const int contig_env = [] {
+    const char *e = getenv("T2SC_CONV_CONTIGUOUS");
+    return e ? atoi(e) : 0;
+  }();
+  static const int bo_env[3] = {
+      getenv("T2SC_BACKOFF_EPI") ? atoi(getenv("T2SC_BACKOFF_EPI")) : 0,
+      getenv("T2SC_BACKOFF_CTL") ? atoi(getenv("T2SC_BACKOFF_CTL")) : 0,
+      getenv("T2SC_BACKOFF_COPY") ? atoi(getenv("T2SC_BACKOFF_COPY")) : 0};
+  a.backoff_epi = bo_env[0];
+  a.backoff_ctl = bo_env[1];
+  a.backoff_copy = bo_env[2];
+  static const int wait_env = getenv("T2SC_WAIT_MODE") ? atoi(getenv("T2SC_WAIT_MODE")) : 0;
+  a.wait_mode = wait_env;
+  a.l1 = l1_env;
+  a.contiguous = contig_env;
   int cols = 32;
   while (cols < 2 * cv->bn) cols <<= 1;
   a.tmem_cols = cols;
@@ -758,9 +856,16 @@ int conv_tc_launch(t2sc_conv *cv, t2sc_map *m, const void *x, void *y, int flags
   int G = 1;
   if (cv->dtype != T2SC_DT_F32)
     while (G < 4 && (int)((G + 1) * a.sub_bytes) <= 48 * 1024 && avail / (int)((G + 1) * a.sub_bytes) >= 4) G++;
+  static const int group_env = getenv("T2SC_CONV_GROUP") ? atoi(getenv("T2SC_CONV_GROUP")) : 0;
+  if (group_env > 0 && cv->dtype != T2SC_DT_F32 && avail / (group_env * (int)a.sub_bytes) >= kMinStages) G = group_env;
   a.group = G;
   a.stage_bytes = G * a.sub_bytes;
   int S = avail / (int)a.stage_bytes;
+  static const int stages_env = [] {
+    const char *e = getenv("T2SC_CONV_STAGES");
+    return e ? atoi(e) : 8;
+  }();
+  if (S > stages_env) S = stages_env;
   if (S > 8) S = 8;
   if (S < kMinStages) {
     err = "conv tile does not fit shared memory";

@@ -72,31 +72,95 @@ __device__ __forceinline__ int32_t hash_find(const int64_t *__restrict__ keys, c
   return -1;
 }
 
-__global__ void neighbor_map_kernel(const int4 *__restrict__ coords, int64_t n, const int64_t *__restrict__ keys,
-                                    const int32_t *__restrict__ vals, uint64_t hmask, int kd, int kh, int kw,
-                                    int dil, int32_t *__restrict__ nbr, uint32_t *__restrict__ mask,
-                                    unsigned long long *__restrict__ n_edges) {
-  int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  uint32_t m = 0;
-  if (r < n) {
-    int4 c = coords[r];
-    int k = 0;
-    for (int kz = 0; kz < kd; kz++)
-      for (int ky = 0; ky < kh; ky++)
-        for (int kx = 0; kx < kw; kx++, k++) {
-          int64_t key = pack_key(c.x, (int64_t)c.y + (int64_t)(kz - kd / 2) * dil,
-                                 (int64_t)c.z + (int64_t)(ky - kh / 2) * dil,
-                                 (int64_t)c.w + (int64_t)(kx - kw / 2) * dil);
-          int32_t hit = hash_find(keys, vals, hmask, key);
-          nbr[(int64_t)k * n + r] = hit;
-          m |= (hit >= 0 ? 1u : 0u) << k;
-        }
-    mask[r] = m;
+// Offset k of a kd x kh x kw kernel moves columns 1, 2, 3 by these amounts.
+__device__ __forceinline__ void offset_of(int k, int kd, int kh, int kw, int dil, int64_t &o1, int64_t &o2,
+                                          int64_t &o3) {
+  const int kz = k / (kh * kw), ky = (k / kw) % kh, kx = k % kw;
+  o1 = (int64_t)(kz - kd / 2) * dil;
+  o2 = (int64_t)(ky - kh / 2) * dil;
+  o3 = (int64_t)(kx - kw / 2) * dil;
+}
+
+// Pass 1: occupancy mask of every target row. One warp per row, lane k
+// probes offset k, so the 27 probes of a row are in flight together; the
+// warp's ballot is the row's mask. Edges are counted per block, then
+// added once to *n_edges.
+__global__ void __launch_bounds__(256) row_mask_kernel(const int4 *__restrict__ coords, int64_t n,
+                                                       const int64_t *__restrict__ keys,
+                                                       const int32_t *__restrict__ vals, uint64_t hmask, int kd,
+                                                       int kh, int kw, int dil, uint32_t *__restrict__ mask,
+                                                       unsigned long long *__restrict__ n_edges) {
+  __shared__ unsigned block_edges;
+  if (threadIdx.x == 0) block_edges = 0;
+  __syncthreads();
+  const int lane = threadIdx.x & 31, K = kd * kh * kw;
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  unsigned cnt = 0;
+  int64_t o1 = 0, o2 = 0, o3 = 0;
+  if (lane < K) offset_of(lane, kd, kh, kw, dil, o1, o2, o3);
+  for (int64_t r = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); r < n; r += warps) {
+    const int4 c = coords[r];
+    bool hit = false;
+    if (lane < K) hit = hash_find(keys, vals, hmask, pack_key(c.x, c.y + o1, c.z + o2, c.w + o3)) >= 0;
+    const uint32_t m = __ballot_sync(0xffffffffu, hit);
+    if (lane == 0) {
+      mask[r] = m;
+      cnt += __popc(m);
+    }
   }
-  // warp-aggregated edge count
-  unsigned cnt = __popc(m);
-  for (int d = 16; d > 0; d >>= 1) cnt += __shfl_down_sync(0xffffffffu, cnt, d);
-  if ((threadIdx.x & 31) == 0 && cnt) atomicAdd(n_edges, (unsigned long long)cnt);
+  if (lane == 0 && cnt) atomicAdd(&block_edges, cnt);
+  __syncthreads();
+  if (threadIdx.x == 0 && block_edges) atomicAdd(n_edges, (unsigned long long)block_edges);
+}
+
+// Pass 2 (after rows are sorted by mask): neighbour rows in sorted order.
+// Block (tile t, offset k) has one thread per tile row p; only offsets the
+// row's mask marks as hits are probed again, the rest are written as -1.
+// nbr_sorted[k][p] is written coalesced; the (t, 0) blocks also write the
+// padded permutation and the tile's offset mask.
+__global__ void __launch_bounds__(kTileRows) sorted_nbr_kernel(const int4 *__restrict__ coords, int64_t n,
+                                                              int64_t n_pad, const int32_t *__restrict__ sorted_rows,
+                                                              const uint32_t *__restrict__ mask,
+                                                              const int64_t *__restrict__ keys,
+                                                              const int32_t *__restrict__ vals, uint64_t hmask,
+                                                              int kd, int kh, int kw, int dil,
+                                                              int32_t *__restrict__ perm_out,
+                                                              int32_t *__restrict__ nbr_sorted,
+                                                              uint32_t *__restrict__ tile_mask) {
+  const int64_t p = (int64_t)blockIdx.x * kTileRows + threadIdx.x;
+  const int k = blockIdx.y;
+  const int32_t row = p < n ? sorted_rows[p] : -1;
+  const uint32_t m = row >= 0 ? mask[row] : 0u;
+  int32_t hit = -1;
+  if ((m >> k) & 1u) {
+    int64_t o1, o2, o3;
+    offset_of(k, kd, kh, kw, dil, o1, o2, o3);
+    const int4 c = coords[row];
+    hit = hash_find(keys, vals, hmask, pack_key(c.x, c.y + o1, c.z + o2, c.w + o3));
+  }
+  nbr_sorted[(int64_t)k * n_pad + p] = hit;
+  if (k == 0) {
+    __shared__ uint32_t wm[kTileRows / 32];
+    perm_out[p] = row;
+    const uint32_t w = __reduce_or_sync(0xffffffffu, m);
+    if ((threadIdx.x & 31) == 0) wm[threadIdx.x >> 5] = w;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      uint32_t t = 0;
+      for (int i = 0; i < kTileRows / 32; i++) t |= wm[i];
+      tile_mask[blockIdx.x] = t;
+    }
+  }
+}
+
+// pos[perm[p]] = p: sorted position of every target row (for the exports,
+// which list edges in the reference's row order).
+__global__ void inverse_perm_kernel(const int32_t *__restrict__ perm, int64_t n_pad, int32_t *__restrict__ pos) {
+  const int64_t p = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (p < n_pad) {
+    const int32_t r = perm[p];
+    if (r >= 0) pos[r] = (int32_t)p;
+  }
 }
 
 __global__ void iota_kernel(int32_t *v, int64_t n) {
@@ -104,46 +168,34 @@ __global__ void iota_kernel(int32_t *v, int64_t n) {
   if (i < n) v[i] = (int32_t)i;
 }
 
-// One 128-thread block per tile: permuted neighbour rows + tile offset mask.
-__global__ void __launch_bounds__(kTileRows) sorted_tiles_kernel(const int32_t *__restrict__ nbr,
-                                                                const uint32_t *__restrict__ mask,
-                                                                const int32_t *__restrict__ perm_in, int64_t n,
-                                                                int64_t n_pad, int kvol,
-                                                                int32_t *__restrict__ perm_out,
-                                                                int32_t *__restrict__ nbr_sorted,
-                                                                uint32_t *__restrict__ tile_mask) {
-  __shared__ uint32_t wm[kTileRows / 32];
-  int64_t p = (int64_t)blockIdx.x * kTileRows + threadIdx.x;
-  int32_t row = p < n ? perm_in[p] : -1;
-  perm_out[p] = row;
-  uint32_t m = row >= 0 ? mask[row] : 0u;
-  for (int k = 0; k < kvol; k++) nbr_sorted[(int64_t)k * n_pad + p] = row >= 0 ? nbr[(int64_t)k * n + row] : -1;
-  m = __reduce_or_sync(0xffffffffu, m);
-  if ((threadIdx.x & 31) == 0) wm[threadIdx.x >> 5] = m;
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    uint32_t t = 0;
-    for (int i = 0; i < kTileRows / 32; i++) t |= wm[i];
-    tile_mask[blockIdx.x] = t;
-  }
-}
-
-__global__ void edge_flags_kernel(const int32_t *__restrict__ nbr, int64_t total, int32_t *__restrict__ flags) {
+// Sort key of a row for the tile order: (row / chunk) in the high bits, the
+// occupancy mask in the low kbits, so rows are grouped by neighbour pattern
+// only inside runs of `chunk` consecutive (spatially close) rows.
+__global__ void chunk_key_kernel(const uint32_t *__restrict__ mask, int64_t n, int64_t chunk, int kbits,
+                                 uint64_t *__restrict__ key) {
   int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (i < total) flags[i] = nbr[i] >= 0 ? 1 : 0;
+  if (i < n) key[i] = ((uint64_t)(i / chunk) << kbits) | mask[i];
 }
 
-__global__ void edge_emit_kernel(const int32_t *__restrict__ nbr, int64_t n, int64_t total,
-                                 const int64_t *__restrict__ pos, int64_t *__restrict__ src,
-                                 int64_t *__restrict__ tgt, int64_t *__restrict__ kidx) {
+__global__ void edge_flags_kernel(const int32_t *__restrict__ nbr_sorted, const int32_t *__restrict__ pos, int64_t n,
+                                  int64_t n_pad, int64_t total, int32_t *__restrict__ flags) {
+  int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < total) flags[i] = nbr_sorted[(i / n) * n_pad + pos[i % n]] >= 0 ? 1 : 0;
+}
+
+// Edges in the reference order: offset-major, target ascending (i = k*n + r).
+__global__ void edge_emit_kernel(const int32_t *__restrict__ nbr_sorted, const int32_t *__restrict__ pos, int64_t n,
+                                 int64_t n_pad, int64_t total, const int64_t *__restrict__ out_pos,
+                                 int64_t *__restrict__ src, int64_t *__restrict__ tgt, int64_t *__restrict__ kidx) {
   int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= total) return;
-  int32_t s = nbr[i];
+  const int64_t k = i / n, r = i % n;
+  int32_t s = nbr_sorted[k * n_pad + pos[r]];
   if (s < 0) return;
-  int64_t p = pos[i];
+  int64_t p = out_pos[i];
   src[p] = s;
-  tgt[p] = i % n;
-  kidx[p] = i / n;
+  tgt[p] = r;
+  kidx[p] = k;
 }
 
 __global__ void row_counts_kernel(const uint32_t *__restrict__ mask, int64_t n, int32_t *__restrict__ cnt) {
@@ -151,17 +203,20 @@ __global__ void row_counts_kernel(const uint32_t *__restrict__ mask, int64_t n, 
   if (r < n) cnt[r] = __popc(mask[r]);
 }
 
-__global__ void csr_emit_kernel(const int32_t *__restrict__ nbr, const uint32_t *__restrict__ mask, int64_t n,
+// CSR rows in target order, kernel index ascending within a row.
+__global__ void csr_emit_kernel(const int32_t *__restrict__ nbr_sorted, const int32_t *__restrict__ pos,
+                                const uint32_t *__restrict__ mask, int64_t n, int64_t n_pad,
                                 const int64_t *__restrict__ row_start, int64_t *__restrict__ src_s,
                                 int64_t *__restrict__ kidx_s) {
   int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (r >= n) return;
   uint32_t m = mask[r];
+  const int64_t q = pos[r];
   int64_t p = row_start[r];
   while (m) {
     int k = __ffs(m) - 1;
     m &= m - 1;
-    src_s[p] = nbr[(int64_t)k * n + r];
+    src_s[p] = nbr_sorted[(int64_t)k * n_pad + q];
     kidx_s[p] = k;
     p++;
   }
@@ -202,48 +257,76 @@ int build_hash(t2sc_coords *c, std::string &err) {
 
 void free_map(t2sc_map *m) {
   if (!m) return;
-  cudaFree(m->nbr);
-  cudaFree(m->mask);
-  cudaFree(m->perm);
-  cudaFree(m->nbr_sorted);
-  cudaFree(m->tile_mask);
+  cudaStream_t st = m->ctx ? m->ctx->stream : nullptr;
+  cudaFreeAsync(m->d_edges, st);
+  cudaFreeAsync(m->mask, st);
+  cudaFreeAsync(m->perm, st);
+  cudaFreeAsync(m->nbr_sorted, st);
+  cudaFreeAsync(m->tile_mask, st);
   delete m;
 }
 
-__global__ void identity_map_kernel(int64_t n, int64_t n_pad, int32_t *__restrict__ nbr, uint32_t *__restrict__ mask,
-                                    int32_t *__restrict__ perm, int32_t *__restrict__ nbr_sorted,
-                                    uint32_t *__restrict__ tile_mask) {
+int map_edges(t2sc_map *m, int64_t *n_edges, std::string &err) {
+  if (m->n_edges < 0) {
+    unsigned long long e = 0;
+    if (m->d_edges) {
+      T2SC_CUDA(cudaMemcpyAsync(&e, m->d_edges, sizeof(e), cudaMemcpyDeviceToHost, m->ctx->stream), "edge count");
+      T2SC_CUDA(cudaStreamSynchronize(m->ctx->stream), "edge count");
+    }
+    m->n_edges = (int64_t)e;
+  }
+  *n_edges = m->n_edges;
+  return T2SC_OK;
+}
+
+// Allocates the arrays of a map with n target rows and kvol offsets from
+// the stream-ordered pool.
+static int alloc_map(t2sc_ctx *ctx, t2sc_map *m, int64_t n, int kvol, std::string &err) {
+  cudaStream_t st = ctx->stream;
+  m->ctx = ctx;
+  m->kvol = kvol;
+  m->n = n;
+  m->ntiles = (n + kTileRows - 1) / kTileRows;
+  m->n_pad = m->ntiles * kTileRows;
+  const size_t np = (size_t)(m->n_pad > 0 ? m->n_pad : 1), nn = (size_t)(n > 0 ? n : 1);
+  T2SC_CUDA(cudaMallocAsync((void **)&m->d_edges, sizeof(unsigned long long), st), "map");
+  T2SC_CUDA(cudaMallocAsync((void **)&m->mask, sizeof(uint32_t) * nn, st), "map mask");
+  T2SC_CUDA(cudaMallocAsync((void **)&m->perm, sizeof(int32_t) * np, st), "map perm");
+  T2SC_CUDA(cudaMallocAsync((void **)&m->nbr_sorted, sizeof(int32_t) * (size_t)kvol * np, st), "map nbr_sorted");
+  T2SC_CUDA(cudaMallocAsync((void **)&m->tile_mask, sizeof(uint32_t) * (size_t)(m->ntiles > 0 ? m->ntiles : 1), st),
+            "map tile_mask");
+  T2SC_CUDA(cudaMemsetAsync(m->d_edges, 0, sizeof(unsigned long long), st), "map");
+  return T2SC_OK;
+}
+
+__global__ void identity_map_kernel(int64_t n, int64_t n_pad, uint32_t *__restrict__ mask, int32_t *__restrict__ perm,
+                                    int32_t *__restrict__ nbr_sorted, uint32_t *__restrict__ tile_mask) {
   const int64_t p = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (p >= n_pad) return;
   const int32_t r = p < n ? (int32_t)p : -1;
   perm[p] = r;
   nbr_sorted[p] = r;
-  if (p < n) nbr[p] = r, mask[p] = 1u;
+  if (p < n) mask[p] = 1u;
   if (p % kTileRows == 0) tile_mask[p / kTileRows] = 1u;  // every tile holds >= 1 row
 }
 
 int build_identity_map(t2sc_ctx *ctx, int64_t n, t2sc_map **out, std::string &err) {
   std::unique_ptr<t2sc_map, void (*)(t2sc_map *)> m(new t2sc_map(), free_map);
-  m->kvol = 1;
-  m->n = m->n_src = m->n_edges = n;
-  m->ntiles = (n + kTileRows - 1) / kTileRows;
-  m->n_pad = m->ntiles * kTileRows;
-  const size_t np = (size_t)(m->n_pad > 0 ? m->n_pad : 1), nn = (size_t)(n > 0 ? n : 1);
-  T2SC_CUDA(cudaMalloc((void **)&m->nbr, sizeof(int32_t) * nn), "identity map");
-  T2SC_CUDA(cudaMalloc((void **)&m->mask, sizeof(uint32_t) * nn), "identity map");
-  T2SC_CUDA(cudaMalloc((void **)&m->perm, sizeof(int32_t) * np), "identity map");
-  T2SC_CUDA(cudaMalloc((void **)&m->nbr_sorted, sizeof(int32_t) * np), "identity map");
-  T2SC_CUDA(cudaMalloc((void **)&m->tile_mask, sizeof(uint32_t) * (size_t)(m->ntiles > 0 ? m->ntiles : 1)),
-            "identity map");
+  int rc = alloc_map(ctx, m.get(), n, 1, err);
+  if (rc != T2SC_OK) return rc;
+  m->n_src = m->n_edges = n;
   if (n > 0) {
-    identity_map_kernel<<<nblk(m->n_pad, 256), 256, 0, ctx->stream>>>(n, m->n_pad, m->nbr, m->mask, m->perm,
-                                                                      m->nbr_sorted, m->tile_mask);
+    identity_map_kernel<<<nblk(m->n_pad, 256), 256, 0, ctx->stream>>>(n, m->n_pad, m->mask, m->perm, m->nbr_sorted,
+                                                                      m->tile_mask);
     T2SC_LAUNCHED(ctx, "identity_map");
   }
   *out = m.release();
   return T2SC_OK;
 }
 
+// Neighbour map of a coordinate set, entirely stream-ordered (no host
+// synchronisation): row masks (one warp per row), rows sorted by mask into
+// 128-row tiles, then the neighbour rows written directly in sorted order.
 int build_map(t2sc_coords *c, int kd, int kh, int kw, int dil, t2sc_map **out, std::string &err) {
   auto key = std::make_tuple(kd, kh, kw, dil);
   auto it = c->maps.find(key);
@@ -255,84 +338,110 @@ int build_map(t2sc_coords *c, int kd, int kh, int kw, int dil, t2sc_map **out, s
   cudaStream_t st = ctx->stream;
   std::unique_ptr<t2sc_map, void (*)(t2sc_map *)> m(new t2sc_map(), free_map);
   const int64_t n = c->n_targets;
-  m->kvol = kd * kh * kw;
-  m->n = n;
+  const int K = kd * kh * kw;
+  int rc = alloc_map(ctx, m.get(), n, K, err);
+  if (rc != T2SC_OK) return rc;
   m->n_src = c->n;
-  m->ntiles = (n + kTileRows - 1) / kTileRows;
-  m->n_pad = m->ntiles * kTileRows;
-  const int K = m->kvol;
-  T2SC_CUDA(cudaMalloc((void **)&m->nbr, sizeof(int32_t) * (size_t)K * (size_t)(n > 0 ? n : 1)), "map nbr");
-  T2SC_CUDA(cudaMalloc((void **)&m->mask, sizeof(uint32_t) * (size_t)(n > 0 ? n : 1)), "map mask");
-  T2SC_CUDA(cudaMalloc((void **)&m->perm, sizeof(int32_t) * (size_t)(m->n_pad > 0 ? m->n_pad : 1)), "map perm");
-  T2SC_CUDA(cudaMalloc((void **)&m->nbr_sorted, sizeof(int32_t) * (size_t)K * (size_t)(m->n_pad > 0 ? m->n_pad : 1)),
-            "map nbr_sorted");
-  T2SC_CUDA(cudaMalloc((void **)&m->tile_mask, sizeof(uint32_t) * (size_t)(m->ntiles > 0 ? m->ntiles : 1)),
-            "map tile_mask");
+  if (n == 0) m->n_edges = 0;
   if (n > 0) {
-    unsigned long long *d_e = nullptr;
-    uint32_t *mask_sorted = nullptr;
-    int32_t *iota = nullptr, *perm_tmp = nullptr;
+    const int4 *tc = (const int4 *)c->d_coords + c->target_begin;
+    const int warps_per_block = 8;
+    const int64_t blocks = std::min<int64_t>((n + warps_per_block - 1) / warps_per_block, (int64_t)ctx->num_sms * 64);
+    row_mask_kernel<<<(unsigned)blocks, 32 * warps_per_block, 0, st>>>(tc, n, c->d_keys, c->d_vals, c->hcap - 1, kd,
+                                                                       kh, kw, dil, m->mask, m->d_edges);
+    T2SC_LAUNCHED(ctx, "row_mask");
+    int32_t *iota = nullptr, *sorted = nullptr;
     void *temp = nullptr;
     size_t temp_bytes = 0;
-    T2SC_CUDA(cudaMallocAsync((void **)&d_e, sizeof(unsigned long long), st), "map scratch");
-    T2SC_CUDA(cudaMemsetAsync(d_e, 0, sizeof(unsigned long long), st), "map scratch");
-    neighbor_map_kernel<<<nblk(n, 128), 128, 0, st>>>((const int4 *)c->d_coords + c->target_begin, n, c->d_keys, c->d_vals,
-                                                       c->hcap - 1, kd, kh, kw, dil, m->nbr, m->mask, d_e);
-    T2SC_LAUNCHED(ctx, "neighbor_map");
-    T2SC_CUDA(cudaMallocAsync((void **)&mask_sorted, sizeof(uint32_t) * n, st), "sort scratch");
     T2SC_CUDA(cudaMallocAsync((void **)&iota, sizeof(int32_t) * n, st), "sort scratch");
-    T2SC_CUDA(cudaMallocAsync((void **)&perm_tmp, sizeof(int32_t) * n, st), "sort scratch");
-    iota_kernel<<<nblk(n, 256), 256, 0, st>>>(iota, n);
+    T2SC_CUDA(cudaMallocAsync((void **)&sorted, sizeof(int32_t) * n, st), "sort scratch");
+    iota_kernel<<<nblk(n, 256), 256, 0, st>>>(ctx->tile_order == kOrderNatural ? sorted : iota, n);
     T2SC_LAUNCHED(ctx, "iota");
-    // stable LSD radix sort of rows by their occupancy mask
-    T2SC_CUDA(cub::DeviceRadixSort::SortPairs(nullptr, temp_bytes, m->mask, mask_sorted, iota, perm_tmp, (int)n, 0,
-                                              K, st),
-              "sort size");
-    T2SC_CUDA(cudaMallocAsync(&temp, temp_bytes, st), "sort scratch");
-    T2SC_CUDA(cub::DeviceRadixSort::SortPairs(temp, temp_bytes, m->mask, mask_sorted, iota, perm_tmp, (int)n, 0, K,
-                                              st),
-              "sort");
-    ctx->launches += 2 * ((K + 7) / 8) + 2;  // approximate CUB launch count (onesweep passes)
-    sorted_tiles_kernel<<<(unsigned)m->ntiles, kTileRows, 0, st>>>(m->nbr, m->mask, perm_tmp, n, m->n_pad, K,
-                                                                    m->perm, m->nbr_sorted, m->tile_mask);
-    T2SC_LAUNCHED(ctx, "sorted_tiles");
-    unsigned long long e = 0;
-    T2SC_CUDA(cudaMemcpyAsync(&e, d_e, sizeof(e), cudaMemcpyDeviceToHost, st), "map edge count");
-    cudaFreeAsync(temp, st);
-    cudaFreeAsync(perm_tmp, st);
+    if (ctx->tile_order == kOrderMask) {
+      // stable LSD radix sort of rows by their occupancy mask (K key bits)
+      uint32_t *mask_sorted = nullptr;
+      T2SC_CUDA(cudaMallocAsync((void **)&mask_sorted, sizeof(uint32_t) * n, st), "sort scratch");
+      T2SC_CUDA(cub::DeviceRadixSort::SortPairs(nullptr, temp_bytes, m->mask, mask_sorted, iota, sorted, (int)n, 0,
+                                                K, st),
+                "sort size");
+      T2SC_CUDA(cudaMallocAsync(&temp, temp_bytes, st), "sort scratch");
+      T2SC_CUDA(cub::DeviceRadixSort::SortPairs(temp, temp_bytes, m->mask, mask_sorted, iota, sorted, (int)n, 0, K,
+                                                st),
+                "sort");
+      ctx->launches += 2 * ((K + 7) / 8) + 2;  // approximate CUB launch count (onesweep passes)
+      cudaFreeAsync(mask_sorted, st);
+    } else if (ctx->tile_order == kOrderChunked) {
+      const int64_t chunk = ctx->tile_chunk > 0 ? ctx->tile_chunk : 1024;
+      int cbits = 1;
+      while (((n + chunk - 1) / chunk) >> cbits) cbits++;
+      uint64_t *keys = nullptr, *keys_sorted = nullptr;
+      T2SC_CUDA(cudaMallocAsync((void **)&keys, sizeof(uint64_t) * n, st), "sort scratch");
+      T2SC_CUDA(cudaMallocAsync((void **)&keys_sorted, sizeof(uint64_t) * n, st), "sort scratch");
+      chunk_key_kernel<<<nblk(n, 256), 256, 0, st>>>(m->mask, n, chunk, K, keys);
+      T2SC_LAUNCHED(ctx, "chunk_key");
+      T2SC_CUDA(cub::DeviceRadixSort::SortPairs(nullptr, temp_bytes, keys, keys_sorted, iota, sorted, (int)n, 0,
+                                                K + cbits, st),
+                "sort size");
+      T2SC_CUDA(cudaMallocAsync(&temp, temp_bytes, st), "sort scratch");
+      T2SC_CUDA(cub::DeviceRadixSort::SortPairs(temp, temp_bytes, keys, keys_sorted, iota, sorted, (int)n, 0,
+                                                K + cbits, st),
+                "sort");
+      ctx->launches += 2 * ((K + cbits + 7) / 8) + 2;
+      cudaFreeAsync(keys, st);
+      cudaFreeAsync(keys_sorted, st);
+    }
+    sorted_nbr_kernel<<<dim3((unsigned)m->ntiles, (unsigned)K), kTileRows, 0, st>>>(
+        tc, n, m->n_pad, sorted, m->mask, c->d_keys, c->d_vals, c->hcap - 1, kd, kh, kw, dil, m->perm,
+        m->nbr_sorted, m->tile_mask);
+    T2SC_LAUNCHED(ctx, "sorted_nbr");
+    if (temp) cudaFreeAsync(temp, st);
+    cudaFreeAsync(sorted, st);
     cudaFreeAsync(iota, st);
-    cudaFreeAsync(mask_sorted, st);
-    cudaFreeAsync(d_e, st);
-    T2SC_CUDA(cudaStreamSynchronize(st), "map build");
-    m->n_edges = (int64_t)e;
   }
   *out = m.get();
   c->maps[key] = m.release();
   return T2SC_OK;
 }
 
+// Sorted position of every target row (stream-ordered scratch).
+static int map_positions(t2sc_ctx *ctx, t2sc_map *m, int32_t **pos, std::string &err) {
+  T2SC_CUDA(cudaMallocAsync((void **)pos, sizeof(int32_t) * (size_t)(m->n > 0 ? m->n : 1), ctx->stream),
+            "export scratch");
+  if (m->n_pad > 0) {
+    inverse_perm_kernel<<<nblk(m->n_pad, 256), 256, 0, ctx->stream>>>(m->perm, m->n_pad, *pos);
+    T2SC_LAUNCHED(ctx, "inverse_perm");
+  }
+  return T2SC_OK;
+}
+
 int export_edges(t2sc_coords *c, t2sc_map *m, int64_t *src, int64_t *tgt, int64_t *kidx, std::string &err) {
   t2sc_ctx *ctx = c->ctx;
   cudaStream_t st = ctx->stream;
-  const int64_t total = (int64_t)m->kvol * m->n, E = m->n_edges;
-  if (E == 0) return T2SC_OK;
-  int32_t *flags = nullptr;
-  int64_t *pos = nullptr, *d_out = nullptr;
-  T2SC_CUDA(cudaMallocAsync((void **)&flags, sizeof(int32_t) * total, st), "export scratch");
-  T2SC_CUDA(cudaMallocAsync((void **)&pos, sizeof(int64_t) * total, st), "export scratch");
-  T2SC_CUDA(cudaMallocAsync((void **)&d_out, sizeof(int64_t) * 3 * E, st), "export scratch");
-  edge_flags_kernel<<<nblk(total, 256), 256, 0, st>>>(m->nbr, total, flags);
-  T2SC_LAUNCHED(ctx, "edge_flags");
-  int rc = scan_counts(ctx, flags, total, pos, nullptr);
+  const int64_t total = (int64_t)m->kvol * m->n;
+  int64_t E = 0;
+  int rc = map_edges(m, &E, err);
   if (rc != T2SC_OK) return rc;
-  edge_emit_kernel<<<nblk(total, 256), 256, 0, st>>>(m->nbr, m->n, total, pos, d_out, d_out + E, d_out + 2 * E);
+  if (E == 0) return T2SC_OK;
+  int32_t *flags = nullptr, *pos = nullptr;
+  int64_t *opos = nullptr, *d_out = nullptr;
+  if ((rc = map_positions(ctx, m, &pos, err)) != T2SC_OK) return rc;
+  T2SC_CUDA(cudaMallocAsync((void **)&flags, sizeof(int32_t) * total, st), "export scratch");
+  T2SC_CUDA(cudaMallocAsync((void **)&opos, sizeof(int64_t) * total, st), "export scratch");
+  T2SC_CUDA(cudaMallocAsync((void **)&d_out, sizeof(int64_t) * 3 * E, st), "export scratch");
+  edge_flags_kernel<<<nblk(total, 256), 256, 0, st>>>(m->nbr_sorted, pos, m->n, m->n_pad, total, flags);
+  T2SC_LAUNCHED(ctx, "edge_flags");
+  rc = scan_counts(ctx, flags, total, opos, nullptr);
+  if (rc != T2SC_OK) return rc;
+  edge_emit_kernel<<<nblk(total, 256), 256, 0, st>>>(m->nbr_sorted, pos, m->n, m->n_pad, total, opos, d_out,
+                                                     d_out + E, d_out + 2 * E);
   T2SC_LAUNCHED(ctx, "edge_emit");
   T2SC_CUDA(cudaMemcpyAsync(src, d_out, sizeof(int64_t) * E, cudaMemcpyDeviceToHost, st), "export copy");
   T2SC_CUDA(cudaMemcpyAsync(tgt, d_out + E, sizeof(int64_t) * E, cudaMemcpyDeviceToHost, st), "export copy");
   T2SC_CUDA(cudaMemcpyAsync(kidx, d_out + 2 * E, sizeof(int64_t) * E, cudaMemcpyDeviceToHost, st), "export copy");
   cudaFreeAsync(flags, st);
-  cudaFreeAsync(pos, st);
+  cudaFreeAsync(opos, st);
   cudaFreeAsync(d_out, st);
+  cudaFreeAsync(pos, st);
   T2SC_CUDA(cudaStreamSynchronize(st), "export");
   return T2SC_OK;
 }
@@ -341,9 +450,13 @@ int export_csr(t2sc_coords *c, t2sc_map *m, int64_t *row_start, int64_t *src_s, 
                std::string &err) {
   t2sc_ctx *ctx = c->ctx;
   cudaStream_t st = ctx->stream;
-  const int64_t n = m->n, E = m->n_edges;
-  int32_t *cnt = nullptr;
+  const int64_t n = m->n;
+  int64_t E = 0;
+  int rc = map_edges(m, &E, err);
+  if (rc != T2SC_OK) return rc;
+  int32_t *cnt = nullptr, *pos = nullptr;
   int64_t *d_rs = nullptr, *d_out = nullptr;
+  if ((rc = map_positions(ctx, m, &pos, err)) != T2SC_OK) return rc;
   T2SC_CUDA(cudaMallocAsync((void **)&cnt, sizeof(int32_t) * (n + 1), st), "csr scratch");
   T2SC_CUDA(cudaMallocAsync((void **)&d_rs, sizeof(int64_t) * (n + 1), st), "csr scratch");
   T2SC_CUDA(cudaMallocAsync((void **)&d_out, sizeof(int64_t) * (2 * E + 1), st), "csr scratch");
@@ -351,10 +464,10 @@ int export_csr(t2sc_coords *c, t2sc_map *m, int64_t *row_start, int64_t *src_s, 
     row_counts_kernel<<<nblk(n, 256), 256, 0, st>>>(m->mask, n, cnt);
     T2SC_LAUNCHED(ctx, "row_counts");
   }
-  int rc = scan_counts(ctx, cnt, n, d_rs, d_rs + n);
+  rc = scan_counts(ctx, cnt, n, d_rs, d_rs + n);
   if (rc != T2SC_OK) return rc;
   if (n > 0) {
-    csr_emit_kernel<<<nblk(n, 256), 256, 0, st>>>(m->nbr, m->mask, n, d_rs, d_out, d_out + E);
+    csr_emit_kernel<<<nblk(n, 256), 256, 0, st>>>(m->nbr_sorted, pos, m->mask, n, m->n_pad, d_rs, d_out, d_out + E);
     T2SC_LAUNCHED(ctx, "csr_emit");
   }
   T2SC_CUDA(cudaMemcpyAsync(row_start, d_rs, sizeof(int64_t) * (n + 1), cudaMemcpyDeviceToHost, st), "csr copy");
@@ -365,6 +478,7 @@ int export_csr(t2sc_coords *c, t2sc_map *m, int64_t *row_start, int64_t *src_s, 
   cudaFreeAsync(cnt, st);
   cudaFreeAsync(d_rs, st);
   cudaFreeAsync(d_out, st);
+  cudaFreeAsync(pos, st);
   T2SC_CUDA(cudaStreamSynchronize(st), "csr export");
   return T2SC_OK;
 }

@@ -15,6 +15,14 @@ namespace t2sc {
 constexpr int kTileRows = 128;  // output rows per conv tile (UMMA M)
 constexpr int kMaxK = 32;       // kernel volume must fit a 32-bit offset mask
 
+// Order of output rows inside conv tiles (a performance choice: the set of
+// terms each output row sums, and their order, do not depend on it).
+enum TileOrder : int {
+  kOrderMask = 0,     // rows sorted by neighbour occupancy mask (fewest wasted MMA rows)
+  kOrderNatural = 1,  // rows in coordinate order (most source-row reuse inside a tile)
+  kOrderChunked = 2,  // mask-sorted inside runs of tile_chunk consecutive rows
+};
+
 // Device-side error flags (bit set by kernels, read by the host after a
 // launch sequence). Kernels never trap; they record and return.
 enum DevErr : int {
@@ -38,22 +46,27 @@ struct t2sc_ctx {
   cudaStream_t stream = nullptr;
   int *d_err = nullptr;      // device error flags (one int)
   int64_t launches = 0;      // kernels launched by this context
+  int tile_order = 0;        // TileOrder of the conv maps built on this context
+  int64_t tile_chunk = 1024; // rows per run for kOrderChunked
   std::string last_error;
   // grow-only staging buffers for the host-pointer entry points
   void *stage[4] = {nullptr, nullptr, nullptr, nullptr};
   size_t stage_cap[4] = {0, 0, 0, 0};
 };
 
-// One neighbour map for a (kernel, dilation) on a coordinate set.
+// One neighbour map for a (kernel, dilation) on a coordinate set. Device
+// arrays come from the context's stream-ordered pool (no synchronising
+// allocation) and are released on the context's stream.
 struct t2sc_map {
+  t2sc_ctx *ctx = nullptr;
   int kvol = 27;
   int64_t n = 0, n_pad = 0, ntiles = 0;  // n: target (output) rows
   int64_t n_src = 0;                      // rows of the input features (targets + halo)
-  int64_t n_edges = 0;
-  int32_t *nbr = nullptr;        // [K][n]    natural row order, -1 = miss
-  uint32_t *mask = nullptr;      // [n]       bit k set iff nbr[k][r] >= 0
+  int64_t n_edges = -1;                   // edge count once read back (-1: still on the device)
+  unsigned long long *d_edges = nullptr;  // device edge count
+  uint32_t *mask = nullptr;      // [n]       bit k set iff target row r has a neighbour at offset k
   int32_t *perm = nullptr;       // [n_pad]   sorted position -> row (-1 padding)
-  int32_t *nbr_sorted = nullptr; // [K][n_pad] nbr in sorted order
+  int32_t *nbr_sorted = nullptr; // [K][n_pad] source row of offset k for sorted position p (-1 = miss)
   uint32_t *tile_mask = nullptr; // [ntiles]  OR of masks in each 128-row tile
 };
 
@@ -89,6 +102,8 @@ namespace t2sc {
 int build_hash(t2sc_coords *c, std::string &err);
 int build_map(t2sc_coords *c, int kd, int kh, int kw, int dil, t2sc_map **out, std::string &err);
 void free_map(t2sc_map *m);
+// Edge count of a map (reads it back from the device once: synchronises).
+int map_edges(t2sc_map *m, int64_t *n_edges, std::string &err);
 // One-offset map with nbr[0][r] = r for rows [0, n): a linear layer run
 // through the conv kernels (dense rows, no coordinates).
 int build_identity_map(t2sc_ctx *ctx, int64_t n, t2sc_map **out, std::string &err);

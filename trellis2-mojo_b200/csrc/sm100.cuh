@@ -67,12 +67,17 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t bar, uint32_t parit
 // Bounded wait: polls until the phase with `parity` completes, another
 // role raised `abort`, or ~`limit_cycles` SM clocks pass (then it raises
 // abort and ORs `err_bit` into *err). Returns false when it gave up.
+// mode 0 polls with the suspend-hinted try_wait, 1 with the plain try_wait,
+// 2 with the non-blocking test_wait.
 __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity, volatile int *abort, int *err,
-                                                  int err_bit, long long limit_cycles) {
+                                                  int err_bit, long long limit_cycles, int mode = 0) {
   if (mbar_test_wait(bar, parity)) return true;
   long long t0 = clock64();
   for (uint32_t i = 1;; i++) {
-    if (mbar_try_wait_sleep(bar, parity)) return true;
+    const bool done = mode == 0   ? mbar_try_wait_sleep(bar, parity)
+                      : mode == 1 ? mbar_try_wait(bar, parity)
+                                  : mbar_test_wait(bar, parity);
+    if (done) return true;
     if ((i & 3) == 0) {
       if (*abort) return false;
       if (clock64() - t0 > limit_cycles) {
@@ -97,6 +102,10 @@ __device__ __forceinline__ void cp_async_16(uint32_t dst, const void *src, uint3
   // no "memory" clobber: the copy's completion is ordered by the mbarrier
   // arrive that follows it, and the address math around it may interleave
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes));
+}
+// Same copy allocating in L1, so rows gathered again soon are served from it.
+__device__ __forceinline__ void cp_async_16_ca(uint32_t dst, const void *src, uint32_t src_bytes) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes));
 }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 template <int N>

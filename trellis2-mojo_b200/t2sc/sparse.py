@@ -342,10 +342,18 @@ class LayerNorm32:
         a new tensor (y may be x). Runs on the context's stream, which is
         ordered after torch's current stream at entry and before it on return."""
         import torch
-        dt = {torch.float32: _lib.DT_F32, torch.float16: _lib.DT_F16, torch.bfloat16: _lib.DT_BF16}[x.dtype]
+        _check_on_ctx_device(x, self.ctx, "LayerNorm32: x")
+        if x.dtype not in (torch.float32, torch.float16, torch.bfloat16):
+            raise ValueError("LayerNorm32: x must be float32, float16 or bfloat16")
+        dt = _torch_dtype_code(x.dtype)
         if x.dim() != 2 or x.shape[1] != self.num_channels or not x.is_contiguous():
             raise ValueError("LayerNorm32: x must be contiguous [rows, num_channels]")
-        y = torch.empty_like(x) if y is None else y
+        if y is None:
+            y = torch.empty_like(x)
+        else:
+            _check_on_ctx_device(y, self.ctx, "LayerNorm32: y")
+            if y.shape != x.shape or y.dtype != x.dtype or not y.is_contiguous():
+                raise ValueError("LayerNorm32: y must be a contiguous tensor of x's shape and dtype")
         w, b = self._wb()
         torch.cuda.current_stream(x.device).synchronize()
         check(lib.t2sc_layernorm_device(self.ctx.handle, ctypes.c_void_p(x.data_ptr()),
@@ -365,6 +373,14 @@ class LayerNorm32:
         return st.replace(y) if st is not None else y
 
     __call__ = forward
+
+
+def _check_on_ctx_device(t, ctx, what):
+    """A device buffer handed to the library must live on the context's GPU:
+    a host tensor or one on another GPU would be read or written through
+    the wrong address space by the kernels."""
+    if not getattr(t, "is_cuda", False) or t.device.index != ctx.device:
+        raise ValueError(f"{what} must be a CUDA tensor on cuda:{ctx.device}")
 
 
 def _torch_dtype_code(t):
@@ -399,8 +415,13 @@ class SparseLinear:
         returns a new [rows, Co] tensor. Runs on the context's stream, ordered
         after torch's current stream at entry and before it on return."""
         import torch
+        _check_on_ctx_device(x, self.ctx, "SparseLinear: x")
+        if residual is not None:
+            _check_on_ctx_device(residual, self.ctx, "SparseLinear: residual")
         if x.dim() != 2 or x.shape[1] != self.in_features or not x.is_contiguous():
             raise ValueError("SparseLinear: x must be contiguous [rows, in_features]")
+        if x.dtype not in (torch.float32, torch.float16, torch.bfloat16):
+            raise ValueError("SparseLinear: x dtype does not match the layer's dtype")
         if _torch_dtype_code(x.dtype) != _DTYPES[self.dtype]:
             raise ValueError("SparseLinear: x dtype does not match the layer's dtype")
         y = torch.empty((x.shape[0], self.out_features), dtype=x.dtype, device=x.device)
