@@ -56,6 +56,57 @@ def inputs():
     return coords, x, ws, bs
 
 
+C5, C5_LAYERS, CFG5_SEEDS = 32, 2, (0, 1, 2, 3)
+CFG5 = ("cfg5: 4 shapes (seeds 0-3), each a 512^3 shell R=200 h=0.5 subdivided with a Bernoulli(0.5) child mask "
+        "(~2.0M voxels at 1024^3), 2 x SubMConv3d(32->32)+SiLU, bf16 in/f32 acc")
+
+
+def cfg5_layers():
+    """Weights of the cfg5 chain (one model shared by the four shapes)."""
+    import t2sc
+    S = t2sc.synth
+    return [(S.normal(521 + 3 * i, (C5, 3, 3, 3, C5), std=(1.0 / (27 * C5)) ** 0.5), S.normal(522 + 3 * i, (C5,), std=0.1))
+            for i in range(C5_LAYERS)]
+
+
+def cfg5_coords(ctx, seed):
+    """Child coordinates of one cfg5 shape: the seeded 512^3 parent shell
+    subdivided on the GPU with a seeded Bernoulli(0.5) child mask."""
+    import t2sc
+    S = t2sc.synth
+    parents = S.shell(*S.SHELLS["cfg5_parent"], seed=seed)
+    mask = S.bernoulli(500 + seed, (len(parents), 8))
+    x0 = np.zeros((len(parents), 8), np.float32)
+    return t2sc.SparseUpsample(2).forward_subdivision(t2sc.SparseTensor(x0, parents, ctx=ctx), mask).coords
+
+
+def conv_launch(L, _lib, ctx, cv, coords_handle, x, y, flags=1, residual=None):
+    _lib.check(L.t2sc_conv_forward_device(cv.handle, coords_handle, ctypes.c_void_p(x.data_ptr()),
+                                          ctypes.c_void_p(y.data_ptr()), flags,
+                                          ctypes.c_void_p(residual.data_ptr()) if residual is not None else None),
+               ctx.handle)
+
+
+def timed(stream, fn, steps, warmup, flush):
+    """W untimed calls, then K calls each bracketed by CUDA events on the
+    launch stream with the L2 flushed before; returns the per-call ms list."""
+    import torch
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    out = []
+    for _ in range(steps):
+        flush.zero_()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        e0.record(stream)
+        fn()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        out.append(e0.elapsed_time(e1))
+    return out
+
+
 class Clocks:
     """nvidia-smi sampling during the timed region."""
 
@@ -200,9 +251,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="t2sc", choices=["t2sc", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--overlap", action="store_true",
-                    help="N>1: convolve interior rows while the halo is in flight (measured slower at N=4 and 8: "
-                         "the second launch per layer costs more than the hidden exchange)")
+    ap.add_argument("--no-extra", action="store_true", help="skip the cfg5 and cfg2 extra keys")
     ap.add_argument("--op", default="conv", choices=["conv", "layernorm"],
                     help="layernorm: time the LayerNorm+SiLU glue kernel alone (not the headline metric)")
     args = ap.parse_args()
@@ -263,6 +312,68 @@ def run_layernorm(args, rows=8_000_000, c=64):
                                  "l2": "inputs larger than L2"},
                       "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": hbm, "peak_source": src,
                                    "unit": "GB/s", "frac": round(gbs / hbm, 3)}}))
+
+
+def extra_single(args, ctx, stream, flush):
+    """cfg5 (the 1024^3 cascade: all four shapes on this GPU) and cfg2's
+    f32 / f16 layers, timed like the headline (CUDA events on the launch
+    stream, L2 flushed between steps). Reported as extra keys."""
+    import torch
+
+    import t2sc
+    from t2sc import _lib
+    L = _lib.lib
+    out = {}
+    peak_tf, peak_bw, _ = peaks()
+    # ---- cfg5: 4 shapes x 2 layers ----
+    convs = [t2sc.SparseConv3d(w, b, dtype="bf16", ctx=ctx) for w, b in cfg5_layers()]
+    shapes, flops, vox = [], 0.0, 0
+    for sd in CFG5_SEEDS:
+        coords = cfg5_coords(ctx, sd)
+        cd = t2sc.Coords(ctx, coords)
+        e = cd.build_map()
+        g = torch.Generator(device="cuda").manual_seed(520 + sd)
+        x = torch.randn((len(coords), C5), device="cuda", generator=g).to(torch.bfloat16)
+        bufs = [torch.empty_like(x) for _ in range(2)]
+        shapes.append((cd, x, bufs))
+        flops += C5_LAYERS * 2.0 * e * C5 * C5
+        vox += len(coords)
+
+    def step5():
+        for cd, x, bufs in shapes:
+            cur = x
+            for i, cv in enumerate(convs):
+                conv_launch(L, _lib, ctx, cv, cd.handle, cur, bufs[i & 1])
+                cur = bufs[i & 1]
+
+    ms = float(np.mean(timed(stream, step5, args.steps, args.warmup, flush)))
+    out.update({"cfg5_tflops": flops / (ms * 1e-3) / 1e12, "cfg5_ms_per_step": ms, "cfg5_voxels": vox,
+                "cfg5_mvoxel_per_s": C5_LAYERS * vox / (ms * 1e-3) / 1e6, "cfg5_frac": flops / (ms * 1e-3) / 1e12 / peak_tf,
+                "cfg5_workload": CFG5})
+    del shapes
+    # ---- cfg2: one SubMConv3d(256->256) layer in f32 (split-TF32) and f16 ----
+    S = t2sc.synth
+    coords = S.shell(*S.SHELLS["cfg2"])
+    n, c = len(coords), 256
+    cd = t2sc.Coords(ctx, coords)
+    e = cd.build_map()
+    w = S.normal(201, (c, 3, 3, 3, c), std=(1.0 / (27 * c)) ** 0.5)
+    b = S.normal(202, (c,), std=0.1)
+    g = torch.Generator(device="cuda").manual_seed(200)
+    x32 = torch.randn((n, c), device="cuda", generator=g)
+    f = 2.0 * e * c * c
+    for dt, tdt, peak, label in (("f32", torch.float32, peak_tf / 6, "TF32x3 = measured bf16 peak / 6"),
+                                 ("f16", torch.float16, peak_tf, "measured bf16 peak")):
+        cv = t2sc.SparseConv3d(w, b, dtype=dt, ctx=ctx)
+        xin = x32.to(tdt)
+        y = torch.empty_like(xin)
+        ms2 = float(np.mean(timed(stream, lambda: conv_launch(L, _lib, ctx, cv, cd.handle, xin, y, 0),
+                                  args.steps, args.warmup, flush)))
+        out[f"cfg2_{dt}_layer_ms"] = ms2
+        out[f"cfg2_{dt}_tflops"] = f / (ms2 * 1e-3) / 1e12
+        out[f"cfg2_{dt}_frac"] = out[f"cfg2_{dt}_tflops"] / peak
+        out[f"cfg2_{dt}_peak"] = label
+    return out
 
 
 def run_single(args):
@@ -367,6 +478,7 @@ def run_single(args):
         e2e_t.append(time.perf_counter() - t0)
     e2e_s = float(np.mean(e2e_t))
 
+    extra = {} if args.no_extra else extra_single(args, ctx, stream, flush)
     cpu = None
     if not args.no_cpu_baseline:
         v, ne, etot, dt = cpu_baseline_sample(coords, x, ws[0], bs[0])
@@ -390,15 +502,22 @@ def run_single(args):
             "gpu_launches": launches,
             "clocks": clk.summary,
             "cpu_baseline": cpu}
+    line.update(extra)
     print(json.dumps(line))
 
 
 def run_distributed(args):
-    """One rank per GPU (torchrun): the cfg4 shell is cut into z-slabs
-    (t2sc.dist); before every layer each rank receives its one-voxel halo
-    from its z-neighbours over NCCL, then convolves (own + halo) rows with
-    outputs for its own rows. Total work is fixed as N grows (strong
-    scaling); `value` is the whole job's TFLOP/s over the slowest rank."""
+    """One rank per GPU (torchrun). cfg4 (the headline): the shell is cut
+    into z-slabs by the library (t2sc_partition_zslab); before every layer
+    each rank receives its one-voxel halo from its z-neighbours through the
+    library's own NCCL communicator (t2sc_halo_exchange_device), then
+    convolves (own + halo) rows with outputs for its own rows. Total work is
+    fixed as N grows (strong scaling); `value` is the whole job's TFLOP/s
+    over the slowest rank. cfg5 (extra keys): the four shapes are spread
+    over the ranks (data parallel), and at N = 8 each shape is z-sharded
+    over a group of two ranks with its own communicator. torch.distributed
+    carries only the plumbing (unique-id broadcast, barriers, max/sum of
+    the timings)."""
     import torch
     import torch.distributed as tdist
 
@@ -413,73 +532,59 @@ def run_distributed(args):
     stream = torch.cuda.Stream()
     torch.cuda.set_stream(stream)
     ctx.set_stream(stream.cuda_stream)
+    L = _lib.lib
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device="cuda")
+
+    # one unique id per communicator: [0] the cfg4 slab group (all ranks),
+    # [1..4] the cfg5 shape groups
+    ids = [dist.Comm.unique_id() for _ in range(1 + len(CFG5_SEEDS))] if rank == 0 else [None]
+    obj = [ids]
+    tdist.broadcast_object_list(obj, src=0)
+    ids = obj[0]
+
+    # ------------------------------- cfg4 -------------------------------
     coords, x, ws, bs = inputs()
-    slab = dist.partition(coords, world)[rank]
-    rows = slab.rows
-    n_own, n_loc = slab.n_own, len(rows)
+    comm = dist.Comm(ctx, ids[0], world, rank)
+    slab = dist.NativeSlab(coords, world, rank)
+    rows, n_own = slab.rows, slab.n_own
+    n_loc = len(rows)
     convs = [t2sc.SparseConv3d(w, b, dtype="bf16", ctx=ctx) for w, b in zip(ws, bs)]
-    n_int = slab.n_int
-    # interior targets [0, n_int) need no halo; boundary targets [n_int, n_own) do
-    c_int = t2sc.Coords(ctx, coords[rows], targets=(0, n_int))
-    c_bnd = t2sc.Coords(ctx, coords[rows], targets=(n_int, n_own))
-    c_all = t2sc.Coords(ctx, coords[rows], n_targets=n_own) if (not args.overlap) else None
+    c_all = t2sc.Coords(ctx, coords[rows], n_targets=n_own)
     torch.cuda.synchronize()
     t0 = time.perf_counter()
-    e_loc = c_int.build_map() + c_bnd.build_map()
-    if c_all is not None:
-        c_all.build_map()
+    e_loc = c_all.build_map()
     torch.cuda.synchronize()
     map_ms = 1e3 * (time.perf_counter() - t0)
     e_all = torch.tensor([e_loc], dtype=torch.int64, device="cuda")
     tdist.all_reduce(e_all)
     E = int(e_all.item())
-
     xin = torch.zeros((n_loc, C), dtype=torch.bfloat16, device="cuda")
     xin[:n_own] = torch.from_numpy(x[slab.own]).to("cuda").to(torch.bfloat16)
     bufs = [torch.zeros((n_loc, C), dtype=torch.bfloat16, device="cuda") for _ in range(2)]
-    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device="cuda")
-    L = _lib.lib
 
     def step():
         cur = xin
         for i, cv in enumerate(convs):
-            pending = dist.start_halo(cur, slab, tdist)  # halo rows of this layer's input
+            comm.exchange(cur, slab.counts)  # halo rows of this layer's input
             out = bufs[i & 1]
-            if (not args.overlap):
-                for q in pending:
-                    q.wait()
-                _lib.check(L.t2sc_conv_forward_device(cv.handle, c_all.handle, ctypes.c_void_p(cur.data_ptr()),
-                                                      ctypes.c_void_p(out.data_ptr()), _lib.SILU, None), ctx.handle)
-                cur = out
-                continue
-            # interior rows while the halo is in flight, boundary rows after it lands
-            _lib.check(L.t2sc_conv_forward_device(cv.handle, c_int.handle, ctypes.c_void_p(cur.data_ptr()),
-                                                  ctypes.c_void_p(out.data_ptr()), _lib.SILU, None), ctx.handle)
-            for q in pending:
-                q.wait()
-            if n_own > n_int:
-                _lib.check(L.t2sc_conv_forward_device(
-                    cv.handle, c_bnd.handle, ctypes.c_void_p(cur.data_ptr()),
-                    ctypes.c_void_p(out.data_ptr() + n_int * C * out.element_size()), _lib.SILU, None), ctx.handle)
+            conv_launch(L, _lib, ctx, cv, c_all.handle, cur, out)
             cur = out
         return cur
 
     for _ in range(args.warmup):
         step()
-    ctx.synchronize()
-    torch.cuda.synchronize()
+    comm.wait()
     # The step (4 x (halo exchange + conv)) is captured once in a CUDA graph:
     # at 4-8 ranks a layer is ~20 us of GPU work, less than the host needs
     # to issue it eagerly. Falls back to eager launches if capture fails.
-    graph = g = None
-    launches_per_step = len(convs) * (2 if n_own > n_int and not (not args.overlap) else 1)
+    graph = None
     try:
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g, stream=stream):
             step()
         torch.cuda.synchronize()
         g.replay()
-        torch.cuda.synchronize()
+        comm.wait()
         graph = g
     except Exception as exc:  # noqa: BLE001
         if rank == 0:
@@ -501,7 +606,7 @@ def run_distributed(args):
         s1.record(stream)
         torch.cuda.synchronize()
         times.append(s0.elapsed_time(s1))
-    launches = ctx.launch_count() - launches0 if graph is None else launches_per_step * args.steps
+    launches = ctx.launch_count() - launches0 if graph is None else len(convs) * args.steps
     t_load = time.perf_counter()
     while time.perf_counter() - t_load < 1.0:
         for _ in range(10):
@@ -518,7 +623,7 @@ def run_distributed(args):
     xh = torch.from_numpy(np.ascontiguousarray(x[slab.own])).pin_memory()
     yh = torch.empty((n_own, C), dtype=torch.float32).pin_memory()
     e2e = []
-    for s in range(args.steps + 2):
+    for s_ in range(args.steps + 2):
         torch.cuda.synchronize()
         tdist.barrier()
         t0 = time.perf_counter()
@@ -527,11 +632,19 @@ def run_distributed(args):
         out = bufs[(len(convs) - 1) & 1]
         yh.copy_(out[:n_own].float(), non_blocking=True)
         torch.cuda.synchronize()
-        if s >= 2:
+        if s_ >= 2:
             e2e.append(time.perf_counter() - t0)
     et = torch.tensor(e2e, dtype=torch.float64, device="cuda")
     tdist.all_reduce(et, op=tdist.ReduceOp.MAX)
     e2e_s = float(et.sum().item()) / args.steps
+    graph = g = None  # noqa: F841  (the graph holds NCCL work of `comm`)
+    torch.cuda.synchronize()
+
+    # ------------------------------- cfg5 -------------------------------
+    extra = {}
+    if not args.no_extra:
+        extra = run_cfg5_distributed(args, ctx, stream, flush, ids, rank, world)
+
     if rank == 0:
         flops = LAYERS * 2.0 * E * C * C
         n = len(coords)
@@ -541,25 +654,123 @@ def run_distributed(args):
                 "mvoxel_per_s": LAYERS * n / (ms * 1e-3) / 1e6, "map_build_ms": map_ms,
                 "config": {"workload": WORKLOAD, "voxels": n, "edges": E, "layers": LAYERS, "channels": C,
                            "l2": "flushed between steps (256 MiB write)",
-                           "parallelism": f"z-slab x{world}, one-voxel halo over NCCL send/recv"
-                                          + (" overlapped with the interior rows' conv" if args.overlap else ""),
+                           "parallelism": f"z-slab x{world}, one-voxel halo over the library's NCCL send/recv",
                            "rank0_rows": n_own, "rank0_halo_rows": n_loc - n_own,
-                           "cuda_graph": graph is not None},
+                           "cuda_graph": run is not step},
                 "e2e": {"value": flops / e2e_s / 1e12, "unit": UNIT, "h2d_bytes_per_step": n * C * 4,
                         "d2h_bytes_per_step": n * C * 4, "ms_per_step": 1e3 * e2e_s},
-                "gpu_launches": launches, "clocks": clk.summary if clk else None, "cpu_baseline": None}
+                "gpu_launches": launches, "clocks": clk.summary if clk else None, "cpu_baseline": None,
+                "gpus_active": world}
+        line.update(extra)
         print(json.dumps(line))
-    # Release the captured graph (it references the NCCL communicator) before
-    # the final barrier, then leave without tearing the communicators down:
-    # destroying a process group whose NCCL comm was captured in a graph can
-    # block, and the process is done.
-    run = graph = g = None  # noqa: F841
-    torch.cuda.synchronize()
-    tdist.barrier()
-    torch.cuda.synchronize()
     sys.stdout.flush()
-    sys.stderr.flush()
-    os._exit(0)
+    teardown(tdist, comm, rank)
+
+
+def teardown(tdist, comm, rank):
+    """Ends a distributed run: the library's communicator is finalised and
+    destroyed (bounded inside the library), then torch's process group. Its
+    teardown has blocked at exit on this pool after the run's work was done,
+    so a watchdog ends the process 30 s after the results were printed if it
+    does not return; each step is logged to stderr with its time."""
+    import threading
+
+    t0 = time.perf_counter()
+
+    def log(msg):
+        print(f"# rank {rank} teardown +{time.perf_counter() - t0:.2f}s: {msg}", file=sys.stderr, flush=True)
+
+    def watchdog():
+        time.sleep(30)
+        log("process-group teardown did not return within 30 s; exiting")
+        os._exit(0)
+
+    threading.Thread(target=watchdog, daemon=True).start()
+    tdist.barrier()
+    comm.close()
+    log("library communicator destroyed")
+    tdist.destroy_process_group()
+    log("process group destroyed")
+
+
+def run_cfg5_distributed(args, ctx, stream, flush, ids, rank, world):
+    """cfg5 over `world` ranks: shapes round-robin when world <= 4, else
+    groups of world // 4 ranks per shape with a z-slab split and a halo
+    exchange per layer on the group's own communicator."""
+    import torch
+    import torch.distributed as tdist
+
+    import t2sc
+    from t2sc import _lib, dist
+    L = _lib.lib
+    convs = [t2sc.SparseConv3d(w, b, dtype="bf16", ctx=ctx) for w, b in cfg5_layers()]
+    nshape = len(CFG5_SEEDS)
+    gs = world // nshape if world > nshape and world % nshape == 0 else 1
+    if gs == 1:
+        mine = [i for i in range(nshape) if i % world == rank]
+    else:
+        mine = [rank // gs]
+    work, comms = [], []
+    e_loc, vox = 0, 0
+    for i in mine:
+        coords = cfg5_coords(ctx, CFG5_SEEDS[i])
+        g = torch.Generator(device="cuda").manual_seed(520 + CFG5_SEEDS[i])
+        xg = torch.randn((len(coords), C5), device="cuda", generator=g).to(torch.bfloat16)
+        if gs == 1:
+            cd = t2sc.Coords(ctx, coords)
+            x, counts, comm = xg, None, None
+        else:
+            comm = dist.Comm(ctx, ids[1 + i], gs, rank % gs)
+            comms.append(comm)
+            sl = dist.NativeSlab(coords, gs, rank % gs)
+            cd = t2sc.Coords(ctx, coords[sl.rows], n_targets=sl.n_own)
+            x = torch.zeros((len(sl.rows), C5), dtype=torch.bfloat16, device="cuda")
+            x[:sl.n_own] = xg[torch.from_numpy(sl.own).cuda()]
+            counts = sl.counts
+        e_loc += cd.build_map()
+        vox += cd.n
+        bufs = [torch.zeros_like(x) for _ in range(2)]
+        work.append((cd, x, bufs, comm, counts))
+
+    def step5():
+        for cd, x, bufs, comm, counts in work:
+            cur = x
+            for j, cv in enumerate(convs):
+                if comm is not None:
+                    comm.exchange(cur, counts)
+                conv_launch(L, _lib, ctx, cv, cd.handle, cur, bufs[j & 1])
+                cur = bufs[j & 1]
+
+    for _ in range(args.warmup):
+        step5()
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(args.steps):
+        flush.zero_()
+        torch.cuda.synchronize()
+        tdist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        step5()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        times.append(e0.elapsed_time(e1))
+    tt = torch.tensor(times, dtype=torch.float64, device="cuda")
+    tdist.all_reduce(tt, op=tdist.ReduceOp.MAX)
+    ms = float(tt.sum().item()) / args.steps
+    tot = torch.tensor([e_loc, vox], dtype=torch.int64, device="cuda")
+    tdist.all_reduce(tot)
+    E5, V5 = int(tot[0].item()), int(tot[1].item())
+    flops = C5_LAYERS * 2.0 * E5 * C5 * C5
+    peak_tf, _, _ = peaks()
+    for comm in comms:
+        comm.close()
+    return {"cfg5_tflops": flops / (ms * 1e-3) / 1e12, "cfg5_ms_per_step": ms, "cfg5_voxels": V5,
+            "cfg5_mvoxel_per_s": C5_LAYERS * V5 / (ms * 1e-3) / 1e6,
+            "cfg5_frac": flops / (ms * 1e-3) / 1e12 / peak_tf / world, "cfg5_workload": CFG5,
+            "cfg5_parallelism": (f"shapes round-robin over {world} ranks" if gs == 1 else
+                                 f"{nshape} groups of {gs} ranks, z-slab + halo inside a group"),
+            "cfg5_scaling": "strong"}
 
 
 if __name__ == "__main__":

@@ -209,6 +209,74 @@ int t2sc_linear_forward_device(t2sc_conv *lin, const void *x, void *y, int64_t r
 int t2sc_layernorm_device(t2sc_ctx *ctx, const void *x, void *y, int64_t rows, int c, const float *w,
                           const float *b, float eps, int flags, int dtype);
 
+/* ---- the decoder's up block: SparseResBlockC2S3d
+ * (trellis2_mojo/models/sc_vaes/sparse_unet_vae.mojo:67-133):
+ *   subdiv = to_subdiv(x) when pred_subdiv (Linear C -> 8), else given;
+ *   h = conv1(SiLU(LN1(x)))            LN1 affine eps 1e-6, conv1 C -> 8*Cout;
+ *   h = C2S(h, subdiv > 0); x2 = C2S(x, subdiv > 0)   (_binarize, :30-37);
+ *   out = conv2(SiLU(LN2(h))) + repeat_interleave(x2, Cout / (C/8))
+ *                                      LN2 no affine eps 1e-6, conv2 Cout -> Cout.
+ * Weights host f32: norm1_w/b [C], conv1 [8*Cout,3,3,3,C] (+ bias [8*Cout]),
+ * conv2 [Cout,3,3,3,Cout] (+ bias), to_subdiv [8,C] (+ bias [8]; NULL when
+ * !pred_subdiv). C % 8 == 0, Cout a multiple of C/8, C and Cout <= 1024. */
+typedef struct t2sc_c2s_block t2sc_c2s_block;
+int t2sc_c2s_block_create(t2sc_ctx *ctx, int channels, int out_channels, int pred_subdiv, const float *norm1_w,
+                          const float *norm1_b, const float *conv1_w, const float *conv1_b, const float *conv2_w,
+                          const float *conv2_b, const float *to_subdiv_w, const float *to_subdiv_b, int dtype,
+                          t2sc_c2s_block **out);
+int t2sc_c2s_block_destroy(t2sc_c2s_block *block);
+/* forward (pred_subdiv: subdiv is an output, device f32 [N, 8]) and
+ * forward_guided (!pred_subdiv: subdiv is the given device f32 [N, 8]).
+ * x: device [N, C] of the block's dtype on `coords` (no halo rows);
+ * out_coords: device int32 [8N, 4]; out_feats: device [8N, Cout] of the
+ * dtype; *m (host) receives the child count M (the call synchronises once
+ * to read it). out_child (nullable) receives a new coordinate handle of the
+ * children with the conv2 map already built, owned by the caller. */
+int t2sc_c2s_block_forward_device(t2sc_c2s_block *block, t2sc_coords *coords, const void *x, float *subdiv,
+                                  int32_t *out_coords, void *out_feats, int64_t *m, t2sc_coords **out_child);
+
+/* ---- multi-GPU data plane (no reference counterpart: the reference is
+ * single-device, trellis2_mojo/gpu/context.mojo:116-165). One process per
+ * GPU. A voxel set is cut into z-slabs of about equal voxel counts; each
+ * rank convolves its own rows plus a halo of its z-neighbours' boundary
+ * planes (t2sc_coords_create_halo with n_targets = counts[0]) and receives
+ * that halo over NCCL before every layer. ---- */
+#define T2SC_COMM_ID_BYTES 128
+typedef struct t2sc_comm t2sc_comm;
+/* The slab of `rank` among `world` (host code, every rank computes its
+ * own). depth = dilation * (kernel / 2) (1 for the decoder's 3^3 convs);
+ * every slab spans >= 2 * depth z planes (else T2SC_ERR_INVALID). rows
+ * (capacity cap, NULL to query the counts) receives global row indices in
+ * local order: interior own rows | own rows of the low band | own rows of
+ * the high band | halo rows from rank - 1 | halo rows from rank + 1, each
+ * group in global order. counts[6] = {own, interior, low band (sent to
+ * rank - 1), high band (sent to rank + 1), halo from rank - 1, halo from
+ * rank + 1}. */
+int t2sc_partition_zslab(const int32_t *coords, int64_t n, int world, int rank, int depth, int64_t *rows,
+                         int64_t cap, int64_t *counts);
+/* A NCCL unique id (T2SC_COMM_ID_BYTES bytes) made by one rank and handed to
+ * the others by the caller's own channel. T2SC_ERR_UNSUPPORTED when
+ * libnccl.so.2 cannot be loaded. */
+int t2sc_comm_unique_id(void *id_out);
+/* Communicator of `nranks` processes on the context's device (NCCL loaded
+ * at run time). Initialisation is polled and bounded by timeout_ms: a peer
+ * that never joins gives T2SC_ERR_TIMEOUT and an aborted communicator. */
+int t2sc_comm_create(t2sc_ctx *ctx, const void *id, int nranks, int rank, int timeout_ms, t2sc_comm **out);
+/* Finalises (bounded) and frees the communicator. */
+int t2sc_comm_destroy(t2sc_comm *comm);
+/* Aborts the communicator's outstanding work (a peer failed). */
+int t2sc_comm_abort(t2sc_comm *comm);
+/* Fills the halo rows of device feats [own + halo rows, row_bytes] from the
+ * z-neighbours: the low band goes to rank - 1 and the high band to rank + 1,
+ * the halo arrives from both, as one grouped send/recv on the context's
+ * stream (asynchronous; capturable in a CUDA graph). counts as returned by
+ * t2sc_partition_zslab. */
+int t2sc_halo_exchange_device(t2sc_comm *comm, void *feats, int64_t row_bytes, const int64_t *counts);
+/* Waits for the context's stream, bounded by timeout_ms while polling the
+ * communicator's asynchronous error state; on a timeout or a NCCL error
+ * the communicator is aborted and T2SC_ERR_TIMEOUT / T2SC_ERR_CUDA returned. */
+int t2sc_comm_wait(t2sc_comm *comm, int timeout_ms);
+
 /* ---- synthetic inputs (seeded shells of the benchmark configurations) ----
  * Active cells of a G^3 grid with | |p-c| - R(1 + 0.1 sin(3t) cos(2(f+phase))) | <= h,
  * c = G/2, t = acos((p_z-c)/|p-c|), f = atan2(p_y-c, p_x-c), phase = 0 for

@@ -204,3 +204,25 @@ def synth_bernoulli(seed, shape, p=0.5):
     out = np.empty(shape, np.float32)
     lib().orc_synth_bernoulli(seed, p, _p(out), out.size)
     return out
+
+
+def c2s_block(coords, x, norm1, conv1, conv2, out_channels, to_subdiv=None, subdiv=None):
+    """SparseResBlockC2S3d._core / forward (trellis2_mojo/models/sc_vaes/
+    sparse_unet_vae.mojo:103-133) composed from the restated pieces:
+    subdiv = to_subdiv(x) (pred path, :126); h = conv1(SiLU(LN1(x))) (:118-119);
+    mask = subdiv > 0 (_binarize, :30-37); h = C2S(h, mask), x2 = C2S(x, mask)
+    (:120-122); h = conv2(SiLU(LN2(h))) (:123-124, LN2 without affine);
+    return h + repeat_interleave(x2) (_skip, :103-115). Returns (coords, h, subdiv)."""
+    x = np.ascontiguousarray(x, np.float32)
+    if subdiv is None:
+        subdiv = linear(x, *to_subdiv)
+    h = layernorm(x, norm1[0], norm1[1], eps=1e-6, silu=True)
+    h = conv(h, conv1[0], conv1[1], neighbor_map(coords))
+    idx, sidx, nc = subdivide(coords, subdiv, positive=True)
+    h = c2s_unfold(h, idx, sidx)
+    x2 = c2s_unfold(x, idx, sidx)
+    h = layernorm(h, None, None, eps=1e-6, silu=True)
+    h = conv(h, conv2[0], conv2[1], neighbor_map(nc))
+    k = out_channels // x2.shape[1]
+    skip = np.repeat(x2, k, axis=1)  # out[r, c*k + j] = x2[r, c]
+    return nc, h + skip, subdiv

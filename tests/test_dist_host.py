@@ -87,3 +87,44 @@ def test_halo_exchange_gloo(world):
     for p in ps:
         p.join(timeout=60)
     assert all(res[r] for r in range(world))
+
+
+@pytest.mark.parametrize("world", [1, 2, 3, 8])
+def test_native_partition_matches_host_mirror(t2sc, world):
+    """t2sc_partition_zslab (the C ABI a Mojo host calls) gives every rank
+    the same rows, order and group sizes as the Python partition."""
+    from t2sc import dist
+    for name in ("cfg1", "cfg2"):
+        coords = t2sc.synth.shell(*t2sc.synth.SHELLS[name])
+        for r, sl in enumerate(dist.partition(coords, world)):
+            ns = dist.NativeSlab(coords, world, r)
+            assert np.array_equal(ns.rows, sl.rows)
+            assert ns.n_own == sl.n_own and ns.n_int == sl.n_int
+            assert ns.counts[2] == sl.lo_send.stop - sl.lo_send.start
+            assert ns.counts[3] == sl.hi_send.stop - sl.hi_send.start
+            assert ns.counts[4] == len(sl.halo_lo) and ns.counts[5] == len(sl.halo_hi)
+
+
+def test_native_partition_rejects_bad_arguments(t2sc):
+    import ctypes
+    from t2sc import _lib
+    coords = t2sc.synth.blob(3)
+    counts = np.zeros(6, np.int64)
+    p, cp = coords.ctypes.data_as(ctypes.c_void_p), counts.ctypes.data_as(ctypes.c_void_p)
+    L = _lib.lib
+    assert L.t2sc_partition_zslab(p, len(coords), 2, 2, 1, None, 0, cp) == _lib.ERR_INVALID   # rank >= world
+    assert L.t2sc_partition_zslab(p, len(coords), 4, 0, 1, None, 0, cp) == _lib.ERR_INVALID   # 3 planes, 4 slabs
+    rows = np.empty(1, np.int64)
+    assert L.t2sc_partition_zslab(p, len(coords), 1, 0, 1, rows.ctypes.data_as(ctypes.c_void_p), 1,
+                                  cp) == _lib.ERR_CAPACITY
+
+
+def test_comm_rejects_bad_arguments(t2sc):
+    import ctypes
+    from t2sc import _lib
+    L = _lib.lib
+    out = ctypes.c_void_p()
+    assert L.t2sc_comm_create(None, None, 2, 0, 1000, ctypes.byref(out)) == _lib.ERR_INVALID
+    assert L.t2sc_halo_exchange_device(None, None, 128, None) == _lib.ERR_INVALID
+    assert L.t2sc_comm_wait(None, 10) == _lib.ERR_INVALID
+    assert L.t2sc_comm_unique_id(None) == _lib.ERR_INVALID

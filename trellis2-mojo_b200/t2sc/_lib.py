@@ -53,6 +53,16 @@ SIGNATURES = {
     "t2sc_linear_create": (I32, [P, P, P, I32, I32, I32, PP]),
     "t2sc_linear_forward_device": (I32, [P, P, P, I64, I32, P]),
     "t2sc_layernorm_device": (I32, [P, P, P, I64, I32, P, P, F, I32, I32]),
+    "t2sc_c2s_block_create": (I32, [P, I32, I32, I32, P, P, P, P, P, P, P, P, I32, PP]),
+    "t2sc_c2s_block_destroy": (I32, [P]),
+    "t2sc_c2s_block_forward_device": (I32, [P, P, P, P, P, P, PI64, PP]),
+    "t2sc_partition_zslab": (I32, [P, I64, I32, I32, I32, P, I64, P]),
+    "t2sc_comm_unique_id": (I32, [P]),
+    "t2sc_comm_create": (I32, [P, P, I32, I32, I32, PP]),
+    "t2sc_comm_destroy": (I32, [P]),
+    "t2sc_comm_abort": (I32, [P]),
+    "t2sc_halo_exchange_device": (I32, [P, P, I64, P]),
+    "t2sc_comm_wait": (I32, [P, I32]),
     "t2sc_synth_shell": (I32, [I32, D, D, U64, I32, P, I64, PI64]),
     "t2sc_synth_normal": (I32, [U64, F, P, I64]),
     "t2sc_synth_bernoulli": (I32, [U64, D, P, I64]),

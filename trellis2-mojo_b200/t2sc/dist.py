@@ -114,3 +114,78 @@ def exchange_halo(feats, slab, dist):
     r + 1, as one grouped batch (ncclGroupStart/End under NCCL)."""
     for q in start_halo(feats, slab, dist):
         q.wait()
+
+
+# ---- the same partition and exchange through the C ABI (what a Mojo host calls) ----
+
+class NativeSlab:
+    """One rank's slab computed by t2sc_partition_zslab: `rows` are global
+    rows in local order (own: interior, low band, high band; then the halo
+    from rank - 1 and from rank + 1) and `counts` the six group sizes the
+    exchange entry point takes."""
+
+    def __init__(self, coords, world, rank, depth=1):
+        import ctypes
+
+        from ._lib import check, lib
+        coords = np.ascontiguousarray(coords, np.int32)
+        self.counts = np.zeros(6, np.int64)
+        p = coords.ctypes.data_as(ctypes.c_void_p)
+        cp = self.counts.ctypes.data_as(ctypes.c_void_p)
+        check(lib.t2sc_partition_zslab(p, len(coords), world, rank, depth, None, 0, cp))
+        total = int(self.counts[0] + self.counts[4] + self.counts[5])
+        self.rows = np.empty(total, np.int64)
+        check(lib.t2sc_partition_zslab(p, len(coords), world, rank, depth,
+                                       self.rows.ctypes.data_as(ctypes.c_void_p), total, cp))
+        self.rank, self.world = rank, world
+        self.n_own, self.n_int = int(self.counts[0]), int(self.counts[1])
+        self.own = self.rows[:self.n_own]
+
+
+class Comm:
+    """A NCCL communicator owned by libt2sc (t2sc_comm_*): the per-layer halo
+    exchange runs inside the library on the context's stream."""
+
+    ID_BYTES = 128
+
+    @staticmethod
+    def unique_id():
+        import ctypes
+
+        from ._lib import check, lib
+        buf = ctypes.create_string_buffer(Comm.ID_BYTES)
+        check(lib.t2sc_comm_unique_id(buf))
+        return buf.raw
+
+    def __init__(self, ctx, uid, nranks, rank, timeout_ms=120000):
+        import ctypes
+
+        from ._lib import check, lib
+        if len(uid) != Comm.ID_BYTES:
+            raise ValueError("Comm: the unique id must be 128 bytes")
+        self.ctx = ctx
+        h = ctypes.c_void_p()
+        check(lib.t2sc_comm_create(ctx.handle, ctypes.create_string_buffer(bytes(uid), Comm.ID_BYTES), nranks, rank,
+                                   timeout_ms, ctypes.byref(h)), ctx.handle)
+        self.handle = h
+
+    def exchange(self, feats, counts):
+        """Halo rows of the device tensor feats [own + halo, C] from the
+        z-neighbours (asynchronous on the context's stream)."""
+        import ctypes
+
+        from ._lib import check, lib
+        counts = np.ascontiguousarray(counts, np.int64)
+        row_bytes = feats.shape[1] * feats.element_size()
+        check(lib.t2sc_halo_exchange_device(self.handle, ctypes.c_void_p(feats.data_ptr()), row_bytes,
+                                            counts.ctypes.data_as(ctypes.c_void_p)), self.ctx.handle)
+
+    def wait(self, timeout_ms=60000):
+        from ._lib import check, lib
+        check(lib.t2sc_comm_wait(self.handle, timeout_ms), self.ctx.handle)
+
+    def close(self):
+        from ._lib import lib
+        if getattr(self, "handle", None):
+            lib.t2sc_comm_destroy(self.handle)
+            self.handle = None

@@ -462,3 +462,72 @@ class SparseLinear:
         if h and self.ctx.handle:
             lib.t2sc_conv_destroy(h)
             self.handle = None
+
+
+class SparseResBlockC2S3d:
+    """The decoder's up block (sparse_unet_vae.mojo:67-133) on the device in
+    one C-ABI call per forward: LN1/SiLU -> conv1 (C -> 8*Cout) -> C2S by the
+    binarized subdivision -> LN2/SiLU -> conv2 + repeat-interleaved C2S of
+    x. Weights as the checkpoint holds them (host f32): norm1 (weight,
+    bias) [C], conv1 [8*Cout, 3, 3, 3, C] + [8*Cout], conv2
+    [Cout, 3, 3, 3, Cout] + [Cout], to_subdiv [8, C] + [8] (pred_subdiv)."""
+
+    def __init__(self, channels, out_channels, pred_subdiv, norm1, conv1, conv2, to_subdiv=None, dtype="f32",
+                 ctx=None):
+        self.channels, self.out_channels, self.pred_subdiv = channels, out_channels, bool(pred_subdiv)
+        self.dtype = dtype
+        self.ctx = ctx or Context.default()
+        f = lambda a: None if a is None else np.ascontiguousarray(a, np.float32)  # noqa: E731
+        self._keep = [f(norm1[0]), f(norm1[1]), f(conv1[0]), f(conv1[1]), f(conv2[0]), f(conv2[1]),
+                      f(to_subdiv[0]) if to_subdiv else None, f(to_subdiv[1]) if to_subdiv else None]
+        if self.pred_subdiv and to_subdiv is None:
+            raise ValueError("SparseResBlockC2S3d: pred_subdiv needs to_subdiv weights")
+        h = ctypes.c_void_p()
+        check(lib.t2sc_c2s_block_create(self.ctx.handle, channels, out_channels, int(self.pred_subdiv),
+                                        *[_p(a) for a in self._keep], _DTYPES[dtype], ctypes.byref(h)),
+              self.ctx.handle)
+        self.handle = h
+
+    def _run(self, x, subdiv=None):
+        import torch
+        if x.feats.shape[1] != self.channels:
+            raise ValueError("SparseResBlockC2S3d: in_features mismatch")
+        n = x.feats.shape[0]
+        dev = f"cuda:{self.ctx.device}"
+        tdt = {"f32": torch.float32, "f16": torch.float16, "bf16": torch.bfloat16}[self.dtype]
+        xd = torch.from_numpy(x.feats).to(dev, tdt)
+        if subdiv is None:
+            sd = torch.empty((n, 8), dtype=torch.float32, device=dev)
+        else:
+            sub = np.ascontiguousarray(subdiv.feats if isinstance(subdiv, SparseTensor) else subdiv, np.float32)
+            if sub.shape != (n, 8):
+                raise ValueError("SparseResBlockC2S3d: subdivision must be [N, 8]")
+            sd = torch.from_numpy(sub).to(dev)
+        oc = torch.empty((8 * max(n, 1), 4), dtype=torch.int32, device=dev)
+        of = torch.empty((8 * max(n, 1), self.out_channels), dtype=tdt, device=dev)
+        m = ctypes.c_int64()
+        torch.cuda.synchronize(dev)
+        check(lib.t2sc_c2s_block_forward_device(self.handle, x.device_coords.handle, ctypes.c_void_p(xd.data_ptr()),
+                                                ctypes.c_void_p(sd.data_ptr()), ctypes.c_void_p(oc.data_ptr()),
+                                                ctypes.c_void_p(of.data_ptr()), ctypes.byref(m), None),
+              self.ctx.handle)
+        self.ctx.synchronize()
+        m = m.value
+        out = SparseTensor(of[:m].float().cpu().numpy(), oc[:m].cpu().numpy(), x.batch_size, self.ctx)
+        return out, sd.cpu().numpy()
+
+    def forward(self, x):
+        """pred_subdiv path: returns (h, subdiv)."""
+        if not self.pred_subdiv:
+            raise ValueError("SparseResBlockC2S3d: use forward_guided when pred_subdiv=False")
+        return self._run(x)
+
+    def forward_guided(self, x, subdiv):
+        """guide_subs path: the subdivision comes from the shape decoder."""
+        return self._run(x, subdiv)[0]
+
+    def __del__(self):
+        h = getattr(self, "handle", None)
+        if h and self.ctx.handle:
+            lib.t2sc_c2s_block_destroy(h)
+            self.handle = None
