@@ -252,11 +252,16 @@ def main():
     ap.add_argument("--impl", default="t2sc", choices=["t2sc", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extra", action="store_true", help="skip the cfg5 and cfg2 extra keys")
-    ap.add_argument("--op", default="conv", choices=["conv", "layernorm"],
-                    help="layernorm: time the LayerNorm+SiLU glue kernel alone (not the headline metric)")
+    ap.add_argument("--op", default="conv", choices=["conv", "layernorm", "map", "subdiv"],
+                    help="layernorm / map / subdiv: time the LayerNorm+SiLU glue kernel, the coordinate hash + "
+                         "neighbour-map build (cfg4) or the subdivision (cfg5 parents) alone (not the headline)")
     args = ap.parse_args()
     if args.op == "layernorm":
         return run_layernorm(args)
+    if args.op == "map":
+        return run_map(args)
+    if args.op == "subdiv":
+        return run_subdiv(args)
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
@@ -264,6 +269,97 @@ def main():
     if args.gpus > 1 or int(os.environ.get("WORLD_SIZE", "1")) > 1:
         return run_distributed(args)
     return run_single(args)
+
+
+def run_map(args):
+    """Coordinate hash + 27-offset neighbour map of the cfg4 shell from
+    device coordinates, as a decoder level pays it when its coordinates
+    change: t2sc_coords_create_device (hash insert + range check) and
+    t2sc_coords_build_map (row masks, mask sort, sorted neighbour rows, edge
+    count). Algorithmic bytes (the survey's B_map): N*16 coords in +
+    N*27*4 map out + 2*cap*12 hash (key + row, written then read)."""
+    import torch
+
+    import t2sc
+    ctx = t2sc.Context.default(0)
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
+    ctx.set_stream(stream.cuda_stream)
+    coords, _, _, _ = inputs()
+    n = len(coords)
+    dc = torch.from_numpy(coords).cuda()
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device="cuda")
+    res = {}
+
+    def once():
+        c = t2sc.Coords(ctx, n=n, device_ptr=dc.data_ptr())
+        res["E"] = c.build_map()
+        del c
+
+    ms = float(np.mean(timed(stream, once, args.steps, max(args.warmup, 3), flush)))
+    cap = 1024
+    while cap < 2 * n:
+        cap *= 2
+    alg = n * 16 + n * 27 * 4 + 2 * cap * 12
+    _, hbm, src = peaks()
+    gbs = alg / (ms * 1e-3) / 1e9
+    print(json.dumps({"metric": "coordinate hash + neighbour-map build, cfg4 shell", "value": round(ms, 4),
+                      "unit": "ms", "n_gpus": 1, "steps": args.steps, "warmup": max(args.warmup, 3),
+                      "higher_is_better": False, "dtype": "int32", "data": "synthetic",
+                      "config": {"workload": f"cfg4 shell, {n} voxels, {res['E']} edges, 3x3x3, from device coords",
+                                 "l2": "flushed between steps (256 MiB write)",
+                                 "includes": "two host synchronisations (hash range check, edge count)"},
+                      "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": hbm, "peak_source": src,
+                                   "unit": "GB/s", "frac": round(gbs / hbm, 4), "algorithmic_bytes": alg}}))
+
+
+def run_subdiv(args):
+    """2x subdivision of one cfg5 parent shell (seed 0, 503,562 parents,
+    Bernoulli(0.5) child mask) with the parents' bf16 C=32 feature rows
+    copied to the ~2M children (t2sc_subdivide_device, one host
+    synchronisation to read M). Algorithmic bytes (the survey's B_sub):
+    N*(16 + 8*4) + M*16 + M*C*2 (+ the N*C*2 parent rows read)."""
+    import torch
+
+    import t2sc
+    from t2sc import _lib
+    ctx = t2sc.Context.default(0)
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
+    ctx.set_stream(stream.cuda_stream)
+    S = t2sc.synth
+    parents = S.shell(*S.SHELLS["cfg5_parent"], seed=0)
+    n = len(parents)
+    dc = torch.from_numpy(parents).cuda()
+    sub = torch.from_numpy(S.bernoulli(500, (n, 8))).cuda()
+    x = torch.randn((n, C5), device="cuda").to(torch.bfloat16)
+    oc = torch.empty((8 * n, 4), dtype=torch.int32, device="cuda")
+    of = torch.empty((8 * n, C5), dtype=torch.bfloat16, device="cuda")
+    par = torch.empty(8 * n, dtype=torch.int32, device="cuda")
+    sidx = torch.empty(8 * n, dtype=torch.int32, device="cuda")
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device="cuda")
+    m = ctypes.c_int64()
+    P = ctypes.c_void_p
+
+    def once():
+        _lib.check(_lib.lib.t2sc_subdivide_device(ctx.handle, P(dc.data_ptr()), n, P(sub.data_ptr()), _lib.SUB_NONZERO,
+                                                  P(x.data_ptr()), C5, _lib.FEATS_UPSAMPLE, _lib.DT_BF16,
+                                                  P(oc.data_ptr()), P(of.data_ptr()), P(par.data_ptr()),
+                                                  P(sidx.data_ptr()), ctypes.byref(m)), ctx.handle)
+
+    ms = float(np.mean(timed(stream, once, args.steps, max(args.warmup, 3), flush)))
+    M = m.value
+    alg = n * (16 + 8 * 4) + M * 16 + M * C5 * 2 + n * C5 * 2
+    _, hbm, src = peaks()
+    gbs = alg / (ms * 1e-3) / 1e9
+    print(json.dumps({"metric": "subdivision upsample, cfg5 parent shell", "value": round(ms, 4), "unit": "ms",
+                      "n_gpus": 1, "steps": args.steps, "warmup": max(args.warmup, 3), "higher_is_better": False,
+                      "dtype": "int32 + bf16 rows", "data": "synthetic",
+                      "config": {"workload": f"{n} parents -> {M} children, C={C5} bf16 feature rows",
+                                 "l2": "flushed between steps (256 MiB write)",
+                                 "includes": "one host synchronisation (child count)"},
+                      "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": hbm, "peak_source": src,
+                                   "unit": "GB/s", "frac": round(gbs / hbm, 4), "algorithmic_bytes": alg}}))
 
 
 def run_layernorm(args, rows=8_000_000, c=64):

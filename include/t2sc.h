@@ -65,7 +65,8 @@ typedef struct t2sc_conv t2sc_conv;
 int t2sc_ctx_create(int device, t2sc_ctx **out);
 int t2sc_ctx_destroy(t2sc_ctx *ctx);
 /* Run this context's work on a caller-owned cudaStream_t (NULL restores the
- * context's own stream). */
+ * context's own stream; cudaStreamLegacy, (void *)1, is the legacy default
+ * stream). */
 int t2sc_ctx_set_stream(t2sc_ctx *ctx, void *cuda_stream);
 int t2sc_ctx_synchronize(t2sc_ctx *ctx);
 const char *t2sc_last_error(const t2sc_ctx *ctx);
@@ -189,8 +190,10 @@ int t2sc_subdivide_noalloc_device(t2sc_ctx *ctx, const int32_t *coords, int64_t 
  * weight f32 [Co, Ci] host, bias f32 [Co] host (nullable); dtype as for
  * convs. The handle is a t2sc_conv with a 1x1x1 kernel (free it with
  * t2sc_conv_destroy) and runs on the same tcgen05 / CUDA-core kernels over
- * an identity row map, built on the first call for a row count and reused
- * while the count stays the same. x device [rows, Ci], y device [rows, Co]
+ * an identity row map, built (stream-ordered, without synchronising) on the
+ * first call with a row count and kept on the context for every linear
+ * layer; the first call with a new count should therefore come before any
+ * stream capture. x device [rows, Ci], y device [rows, Co]
  * (must not alias x), flags T2SC_SILU / T2SC_RESIDUAL (residual [rows, Co])
  * fused into the epilogue, so lin2(silu(lin1(h))) + x is two calls. */
 int t2sc_linear_create(t2sc_ctx *ctx, const float *weight, const float *bias, int co, int ci, int dtype,
@@ -208,6 +211,19 @@ int t2sc_linear_forward_device(t2sc_conv *lin, const void *x, void *y, int64_t r
  * SiLU; statistics in f32. 1 <= c <= 1024. Asynchronous on the stream. */
 int t2sc_layernorm_device(t2sc_ctx *ctx, const void *x, void *y, int64_t rows, int c, const float *w,
                           const float *b, float eps, int flags, int dtype);
+
+/* ---- the decoder's stage block: SparseConvNeXtBlock3d
+ * (trellis2_mojo/models/sc_vaes/sparse_unet_vae.mojo:40-64):
+ *   y = lin2(SiLU(lin1(LN(conv(x))))) + x, LN affine eps 1e-6.
+ * Weights host f32: conv [C,3,3,3,C] (+ bias [C]), norm w/b [C], lin1 [H,C]
+ * (+ [H]), lin2 [C,H] (+ [C]). x, y: device [N, C] of dtype on `coords`
+ * (no halo rows), y must not alias x. Asynchronous on the stream. */
+typedef struct t2sc_convnext_block t2sc_convnext_block;
+int t2sc_convnext_block_create(t2sc_ctx *ctx, int channels, int hidden, const float *conv_w, const float *conv_b,
+                               const float *norm_w, const float *norm_b, const float *lin1_w, const float *lin1_b,
+                               const float *lin2_w, const float *lin2_b, int dtype, t2sc_convnext_block **out);
+int t2sc_convnext_block_destroy(t2sc_convnext_block *block);
+int t2sc_convnext_block_forward_device(t2sc_convnext_block *block, t2sc_coords *coords, const void *x, void *y);
 
 /* ---- the decoder's up block: SparseResBlockC2S3d
  * (trellis2_mojo/models/sc_vaes/sparse_unet_vae.mojo:67-133):

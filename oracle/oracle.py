@@ -226,3 +226,40 @@ def c2s_block(coords, x, norm1, conv1, conv2, out_channels, to_subdiv=None, subd
     k = out_channels // x2.shape[1]
     skip = np.repeat(x2, k, axis=1)  # out[r, c*k + j] = x2[r, c]
     return nc, h + skip, subdiv
+
+
+def convnext_block(coords, x, conv_wb, norm_wb, lin1_wb, lin2_wb, edges=None):
+    """SparseConvNeXtBlock3d.forward (sparse_unet_vae.mojo:60-64): conv ->
+    LayerNorm(affine, eps 1e-6) -> lin2(SiLU(lin1(h))) -> + x."""
+    h = conv(x, conv_wb[0], conv_wb[1], edges if edges is not None else neighbor_map(coords))
+    h = layernorm(h, norm_wb[0], norm_wb[1], eps=1e-6)
+    h = linear(h, lin1_wb[0], lin1_wb[1], silu=True)
+    return linear(h, lin2_wb[0], lin2_wb[1], residual=x)
+
+
+def decoder(sd, model_channels, num_blocks, coords, x, guide_subs=None, pred_subdiv=True):
+    """SparseUnetVaeDecoder.forward / forward_guided (sparse_unet_vae.mojo:
+    172-206, weights named as sparse_unet_vae_decoder_from, :255-284):
+    from_latent -> per stage its ConvNeXt blocks, then (except the last
+    stage) the C2S up block -> LayerNorm (eps 1e-5, no affine) ->
+    output_layer. With guide_subs the up blocks use them (forward_guided);
+    with pred_subdiv the predicted subdivisions are returned as well.
+    Returns (coords, feats, subs)."""
+    g = lambda n: (sd[n + ".weight"], sd.get(n + ".bias"))  # noqa: E731
+    h = linear(x, *g("from_latent"))
+    subs = []
+    for s in range(len(num_blocks)):
+        edges = neighbor_map(coords)
+        for j in range(num_blocks[s]):
+            p = f"blocks.{s}.{j}"
+            h = convnext_block(coords, h, g(p + ".conv"), g(p + ".norm"), g(p + ".mlp.0"), g(p + ".mlp.2"), edges)
+        if s < len(num_blocks) - 1:
+            p = f"blocks.{s}.{num_blocks[s]}"
+            given = None if guide_subs is None else guide_subs[s]
+            pred = linear(h, *g(p + ".to_subdiv")) if pred_subdiv else None   # forward, :126-130
+            use = given if given is not None else pred
+            coords, h, _ = c2s_block(coords, h, g(p + ".norm1"), g(p + ".conv1"), g(p + ".conv2"),
+                                     model_channels[s + 1], subdiv=use)
+            subs.append(pred if pred_subdiv else use)
+    h = layernorm(h, None, None, eps=1e-5)
+    return coords, linear(h, *g("output_layer")), subs

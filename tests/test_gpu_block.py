@@ -58,3 +58,21 @@ def test_c2s_block_rejects_bad_shapes(t2sc):
         t2sc.SparseResBlockC2S3d(60, 32, True, (norm1[0][:60], norm1[1][:60]), conv1, conv2, to_sub)
     with pytest.raises(ValueError):
         t2sc.SparseResBlockC2S3d(64, 32, True, norm1, conv1, conv2, None)
+
+
+def test_convnext_block_entry_point_f32(t2sc, oracle):
+    """SparseConvNeXtBlock3d as one device call (conv -> LN -> lin1/SiLU ->
+    lin2 + x) against oracle.convnext_block."""
+    import torch
+    S = t2sc.synth
+    coords = S.shell(*S.SHELLS["cfg1"])
+    c = 64
+    x = S.normal(990, (len(coords), c))
+    conv = (S.normal(991, (c, 3, 3, 3, c), std=(27 * c) ** -0.5), S.normal(992, (c,), std=0.1))
+    norm = (1 + 0.1 * S.normal(993, (c,)), 0.1 * S.normal(994, (c,)))
+    lin1 = (S.normal(995, (4 * c, c), std=c ** -0.5), S.normal(996, (4 * c,), std=0.1))
+    lin2 = (S.normal(997, (c, 4 * c), std=(4 * c) ** -0.5), S.normal(998, (c,), std=0.1))
+    blk = t2sc.SparseConvNeXtBlock3d(c, conv, norm, lin1, lin2)
+    xt = t2sc.SparseTensor(x, coords)
+    y = blk.forward_device(xt.device_coords, torch.from_numpy(x).cuda()).cpu().numpy()
+    assert rel_err(y, oracle.convnext_block(coords, x, conv, norm, lin1, lin2)) <= F32_TOL

@@ -131,6 +131,9 @@ int t2sc_ctx_destroy(t2sc_ctx *ctx) {
   if (!ctx) return T2SC_OK;
   DeviceGuard g(ctx->device);
   cudaStreamSynchronize(ctx->stream);
+  for (void *p : ctx->stage)
+    if (p) cudaFree(p);
+  for (auto &kv : ctx->id_maps) free_map(kv.second);
   cudaFree(ctx->d_err);
   if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
   delete ctx;
@@ -175,7 +178,7 @@ static int coords_create_impl(t2sc_ctx *ctx, const int32_t *coords, int64_t n, i
     c->n = n;
     c->n_targets = n_targets;
     c->target_begin = target_begin;
-    T2SC_CUDA(cudaMalloc((void **)&c->d_coords, (size_t)(n > 0 ? n : 1) * 16), "coords");
+    T2SC_CUDA(cudaMallocAsync((void **)&c->d_coords, (size_t)(n > 0 ? n : 1) * 16, ctx->stream), "coords");
     if (n > 0)
       T2SC_CUDA(cudaMemcpyAsync(c->d_coords, coords, (size_t)n * 16,
                                 on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, ctx->stream),
@@ -209,11 +212,11 @@ int t2sc_coords_create_range(t2sc_ctx *ctx, const int32_t *coords, int64_t n, in
 int t2sc_coords_destroy(t2sc_coords *c) {
   if (!c) return T2SC_OK;
   DeviceGuard g(c->ctx->device);
-  cudaStreamSynchronize(c->ctx->stream);
+  // stream-ordered release: work already queued on the context's stream
+  // that reads these buffers still runs first, and nothing synchronises
   for (auto &kv : c->maps) free_map(kv.second);
-  cudaFree(c->d_coords);
-  cudaFree(c->d_keys);
-  cudaFree(c->d_vals);
+  cudaFreeAsync(c->d_coords, c->ctx->stream);
+  cudaFreeAsync(c->d_slots, c->ctx->stream);
   delete c;
   return T2SC_OK;
 }
@@ -336,7 +339,6 @@ int t2sc_conv_destroy(t2sc_conv *cv) {
   cudaFree(cv->d_wtc);
   cudaFree(cv->d_w_simt);
   cudaFree(cv->d_w_lo);
-  free_map(cv->lin_map);
   delete cv;
   return T2SC_OK;
 }
@@ -373,14 +375,12 @@ int t2sc_linear_forward_device(t2sc_conv *lin, const void *x, void *y, int64_t r
   if (rows == 0) return T2SC_OK;
   return guarded(ctx, [&]() -> int {
     DeviceGuard g(ctx->device);
-    if (!lin->lin_map || lin->lin_map->n != rows) {
-      cudaStreamSynchronize(ctx->stream);  // the old map may still be read by a launch in flight
-      free_map(lin->lin_map);
-      lin->lin_map = nullptr;
-      T2SC_TRY(build_identity_map(ctx, rows, &lin->lin_map, ctx->last_error));
-    }
-    return lin->tc_path ? conv_tc_launch(lin, lin->lin_map, x, y, flags, residual, ctx->last_error)
-                        : conv_simt_launch(lin, lin->lin_map, x, y, flags, residual, ctx->last_error);
+    // identity map of this row count: built once per context (stream-ordered,
+    // no synchronisation) and shared by all linear layers
+    t2sc_map *&im = ctx->id_maps[rows];
+    if (!im) T2SC_TRY(build_identity_map(ctx, rows, &im, ctx->last_error));
+    return lin->tc_path ? conv_tc_launch(lin, im, x, y, flags, residual, ctx->last_error)
+                        : conv_simt_launch(lin, im, x, y, flags, residual, ctx->last_error);
   });
 }
 

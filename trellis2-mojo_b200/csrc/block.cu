@@ -176,3 +176,97 @@ int t2sc_c2s_block_forward_device(t2sc_c2s_block *b, t2sc_coords *coords, const 
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// SparseConvNeXtBlock3d (sparse_unet_vae.mojo:40-64):
+//   y = lin2(SiLU(lin1(LN(conv(x))))) + x,  LN affine eps 1e-6.
+// Four kernels on the context's stream: the conv, LayerNorm in place, lin1
+// with SiLU fused, lin2 with the residual x fused into its epilogue.
+
+struct t2sc_convnext_block {
+  t2sc_ctx *ctx = nullptr;
+  int channels = 0, hidden = 0, dtype = 0;
+  float *d_norm = nullptr;  // [2, C]
+  t2sc_conv *conv = nullptr, *lin1 = nullptr, *lin2 = nullptr;
+};
+
+extern "C" {
+
+int t2sc_convnext_block_create(t2sc_ctx *ctx, int channels, int hidden, const float *conv_w, const float *conv_b,
+                               const float *norm_w, const float *norm_b, const float *lin1_w, const float *lin1_b,
+                               const float *lin2_w, const float *lin2_b, int dtype, t2sc_convnext_block **out) {
+  if (!ctx || !out) return T2SC_ERR_INVALID;
+  *out = nullptr;
+  if (channels < 1 || channels > 1024 || hidden < 1)
+    return fail(ctx, T2SC_ERR_INVALID, "convnext block: need 1 <= C <= 1024 (LayerNorm width) and hidden >= 1");
+  if (!conv_w || !norm_w || !norm_b || !lin1_w || !lin2_w)
+    return fail(ctx, T2SC_ERR_INVALID, "convnext block: null weight");
+  std::unique_ptr<t2sc_convnext_block, int (*)(t2sc_convnext_block *)> b(new t2sc_convnext_block(),
+                                                                         t2sc_convnext_block_destroy);
+  b->ctx = ctx;
+  b->channels = channels;
+  b->hidden = hidden;
+  b->dtype = dtype;
+  int prev = -1;
+  cudaGetDevice(&prev);
+  cudaSetDevice(ctx->device);
+  std::vector<float> wb(2 * (size_t)channels);
+  for (int i = 0; i < channels; i++) wb[i] = norm_w[i], wb[channels + i] = norm_b[i];
+  int rc = T2SC_OK;
+  if (cudaMalloc((void **)&b->d_norm, wb.size() * 4) != cudaSuccess ||
+      cudaMemcpy(b->d_norm, wb.data(), wb.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess)
+    rc = fail(ctx, T2SC_ERR_OOM, "convnext block: norm weights");
+  if (rc == T2SC_OK) rc = t2sc_conv_create(ctx, conv_w, conv_b, channels, 3, 3, 3, channels, 1, dtype, &b->conv);
+  if (rc == T2SC_OK) rc = t2sc_linear_create(ctx, lin1_w, lin1_b, hidden, channels, dtype, &b->lin1);
+  if (rc == T2SC_OK) rc = t2sc_linear_create(ctx, lin2_w, lin2_b, channels, hidden, dtype, &b->lin2);
+  if (prev >= 0) cudaSetDevice(prev);
+  if (rc != T2SC_OK) return rc;
+  *out = b.release();
+  return T2SC_OK;
+}
+
+int t2sc_convnext_block_destroy(t2sc_convnext_block *b) {
+  if (!b) return T2SC_OK;
+  t2sc_conv_destroy(b->conv);
+  t2sc_conv_destroy(b->lin1);
+  t2sc_conv_destroy(b->lin2);
+  if (b->d_norm) cudaFree(b->d_norm);
+  delete b;
+  return T2SC_OK;
+}
+
+int t2sc_convnext_block_forward_device(t2sc_convnext_block *b, t2sc_coords *coords, const void *x, void *y) {
+  if (!b || !coords) return T2SC_ERR_INVALID;
+  t2sc_ctx *ctx = b->ctx;
+  if (coords->ctx != ctx) return fail(ctx, T2SC_ERR_INVALID, "convnext block: coords of another context");
+  if (coords->n_targets != coords->n || coords->target_begin != 0)
+    return fail(ctx, T2SC_ERR_INVALID, "convnext block: coordinates with halo rows are not supported");
+  const int64_t n = coords->n;
+  if (n == 0) return T2SC_OK;
+  if (!x || !y || x == y) return fail(ctx, T2SC_ERR_INVALID, "convnext block: null or aliased buffers");
+  int prev = -1;
+  cudaGetDevice(&prev);
+  cudaSetDevice(ctx->device);
+  std::string &err = ctx->last_error;
+  cudaStream_t st = ctx->stream;
+  const size_t es = b->dtype == T2SC_DT_F32 ? 4 : 2;
+  void *h1 = nullptr, *h2 = nullptr;
+  auto body = [&]() -> int {
+    T2SC_CUDA(cudaMallocAsync(&h1, (size_t)n * b->channels * es, st), "convnext scratch");
+    T2SC_CUDA(cudaMallocAsync(&h2, (size_t)n * b->hidden * es, st), "convnext scratch");
+    int rc;
+    if ((rc = t2sc_conv_forward_device(b->conv, coords, x, h1, 0, nullptr)) != T2SC_OK) return rc;
+    if ((rc = t2sc_layernorm_device(ctx, h1, h1, n, b->channels, b->d_norm, b->d_norm + b->channels, kBlockEps, 0,
+                                    b->dtype)) != T2SC_OK)
+      return rc;
+    if ((rc = t2sc_linear_forward_device(b->lin1, h1, h2, n, T2SC_SILU, nullptr)) != T2SC_OK) return rc;
+    return t2sc_linear_forward_device(b->lin2, h2, y, n, T2SC_RESIDUAL, x);
+  };
+  int rc = body();
+  if (h1) cudaFreeAsync(h1, st);
+  if (h2) cudaFreeAsync(h2, st);
+  if (prev >= 0) cudaSetDevice(prev);
+  return rc;
+}
+
+}  // extern "C"

@@ -100,8 +100,9 @@ struct TcArgs {
 #endif
   int l1;          // gather through L1 (cp.async.ca) instead of L2 only (.cg)
   int contiguous;  // CTA b takes units [b*U/G, (b+1)*U/G) instead of b, b+G, b+2G, ...
-  uint32_t backoff_epi, backoff_ctl, backoff_copy;
-  int wait_mode;  // how a waiting thread polls an mbarrier (sm100::mbar_wait_bounded)  // sleep between polls of a waiting warp (ns; 0 = spin)
+  uint32_t backoff_epi, backoff_ctl, backoff_copy;  // sleep between polls of a waiting warp (ns; 0 = spin)
+  int wait_mode;   // how a waiting thread polls an mbarrier (sm100::mbar_wait_bounded)
+  int wait_elect;  // warps wait with one polling lane (1) or with every lane (0)
   int *err;
 };
 // Diagnostics build only (-DT2SC_CONV_DIAGNOSTICS=1, never the product
@@ -206,7 +207,18 @@ __device__ __forceinline__ void store16(const TcArgs &a, int orow, int col, cons
 // leaves the issue slots to the working ones, and the other lanes then
 // observe the completed phase themselves (each consumer lane acquires it).
 __device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, volatile int *abort, int *err,
-                                          uint32_t backoff_ns = 0, int g_wait_mode = 0) {
+                                          uint32_t backoff_ns = 0, int g_wait_mode = 0, int elect = 0) {
+  if (elect) {
+    // lane 0 alone polls (one barrier operation per poll instead of 32);
+    // the warp barrier then orders the other lanes' later accesses after
+    // the phase lane 0 observed
+    bool ok = true;
+    if ((threadIdx.x & 31) == 0 && !sm100::mbar_test_wait(bar, parity))
+      ok = sm100::mbar_wait_bounded(bar, parity, abort, err, kDevErrTimeout, kWaitLimit, g_wait_mode);
+    ok = __shfl_sync(0xffffffffu, ok, 0);
+    __syncwarp();
+    return ok;
+  }
   bool ok = sm100::mbar_test_wait(bar, parity);
   if (__all_sync(0xffffffffu, ok)) return true;
   if (backoff_ns == 0) {
@@ -331,7 +343,7 @@ __global__ void __launch_bounds__(Roles<DT, RB>::kThreads, 1)
       uint32_t km = km_next;
       km_next = mask_of(unit_at(i + 1));
       const int npairs = __popc(km) * a.nchunks;
-      if (npairs > 0 && !warp_wait(idxf0 + 8 * (t & 1), (t >> 1) & 1, abort, a.err, 0, a.wait_mode)) {
+      if (npairs > 0 && !warp_wait(idxf0 + 8 * (t & 1), (t >> 1) & 1, abort, a.err, 0, a.wait_mode, a.wait_elect)) {
         ok = false;
         break;
       }
@@ -341,7 +353,7 @@ __global__ void __launch_bounds__(Roles<DT, RB>::kThreads, 1)
       uint32_t gs[RPL];
       for (int q = 0; q < npairs && ok;) {
         if (tid == 32 * kCopyWarp0) T2SC_TRACE(0, cit);
-        if (!warp_wait(empty0 + 8 * s, ph ^ 1, abort, a.err, a.backoff_copy, a.wait_mode)) {
+        if (!warp_wait(empty0 + 8 * s, ph ^ 1, abort, a.err, a.backoff_copy, a.wait_mode, a.wait_elect)) {
           ok = false;
           break;
         }
@@ -372,6 +384,7 @@ __global__ void __launch_bounds__(Roles<DT, RB>::kThreads, 1)
               gs[p] = src[p] >= 0 ? 16u : 0u;
             }
           }
+          if (tid == 32 * kCopyWarp0) T2SC_TRACE(10, cit);
           const uint32_t sub = abase + g * a.sub_bytes;
           const bool cvalid = c * BKE + j * EPV < a.ci;
 #pragma unroll
@@ -387,6 +400,7 @@ __global__ void __launch_bounds__(Roles<DT, RB>::kThreads, 1)
             }
           }
         }
+        if (tid == 32 * kCopyWarp0) T2SC_TRACE(11, cit);
         // arrives on the stage barrier once this lane's copies have landed
         sm100::cp_async_arrive_noinc(bar);
         if (tid == 32 * kCopyWarp0) T2SC_TRACE(6, cit);
@@ -432,7 +446,7 @@ __global__ void __launch_bounds__(Roles<DT, RB>::kThreads, 1)
       if (u_next < nunits) {
         // the other buffer held unit t-1: wait until every copy warp is done with it
         const uint32_t nb = (t + 1) & 1;
-        if (!warp_wait(idxe0 + 8 * nb, (((t + 1) >> 1) & 1) ^ 1, abort, a.err, a.backoff_ctl, a.wait_mode)) {
+        if (!warp_wait(idxe0 + 8 * nb, (((t + 1) >> 1) & 1) ^ 1, abort, a.err, a.backoff_ctl, a.wait_mode, a.wait_elect)) {
           ok = false;
           break;
         }
@@ -448,7 +462,7 @@ __global__ void __launch_bounds__(Roles<DT, RB>::kThreads, 1)
       const uint8_t *wk = a.wimg;
       for (int q = 0; q < npairs && ok;) {
         if (lane == 0) T2SC_TRACE(7, it);
-        if (!warp_wait(empty0 + 8 * s, ph ^ 1, abort, a.err, a.backoff_ctl, a.wait_mode)) {
+        if (!warp_wait(empty0 + 8 * s, ph ^ 1, abort, a.err, a.backoff_ctl, a.wait_mode, a.wait_elect)) {
           ok = false;
           break;
         }
@@ -521,7 +535,7 @@ __global__ void __launch_bounds__(Roles<DT, RB>::kThreads, 1)
         bool ok = true;
         for (int kk = __popc(km); kk > 0; kk--) {
           const uint32_t b = acc_it & 1;
-          if (!warp_wait(tfull0 + 8 * b, (acc_it >> 1) & 1, abort, a.err, a.backoff_epi, a.wait_mode)) {
+          if (!warp_wait(tfull0 + 8 * b, (acc_it >> 1) & 1, abort, a.err, a.backoff_epi, a.wait_mode, a.wait_elect)) {
             ok = false;
             break;
           }
@@ -558,7 +572,7 @@ __global__ void __launch_bounds__(Roles<DT, RB>::kThreads, 1)
       }
       const uint32_t b = acc_it & 1;
       if (tid == 0) T2SC_TRACE(4, acc_it);
-      if (!warp_wait(tfull0 + 8 * b, (acc_it >> 1) & 1, abort, a.err, a.backoff_epi, a.wait_mode)) break;
+      if (!warp_wait(tfull0 + 8 * b, (acc_it >> 1) & 1, abort, a.err, a.backoff_epi, a.wait_mode, a.wait_elect)) break;
       if (tid == 0) T2SC_TRACE(5, acc_it);
       sm100::tc_fence_after();
       const uint32_t tbase = tmem + ((uint32_t)(32 * q) << 16) + b * a.bn;
@@ -692,12 +706,12 @@ int launch_tc(t2sc_conv *cv, const TcArgs &args, int grid, size_t smem, std::str
   const char *trace_path = getenv("T2SC_CONV_TRACE");
   if (trace_path) {  // diagnostics only: allocates, synchronises and writes a file
     TcArgs t = args;
-    const size_t bytes = 10 * kTraceN * sizeof(long long);
+    const size_t bytes = 12 * kTraceN * sizeof(long long);
     T2SC_CUDA(cudaMalloc((void **)&t.trace, bytes), "trace");
     T2SC_CUDA(cudaMemset(t.trace, 0, bytes), "trace");
     kfn<<<grid, Roles<DT, RB>::kThreads, smem, cv->ctx->stream>>>(t);
     T2SC_LAUNCHED(cv->ctx, "conv_tc");
-    std::vector<long long> h(10 * kTraceN);
+    std::vector<long long> h(12 * kTraceN);
     T2SC_CUDA(cudaMemcpyAsync(h.data(), t.trace, bytes, cudaMemcpyDeviceToHost, cv->ctx->stream), "trace");
     T2SC_CUDA(cudaStreamSynchronize(cv->ctx->stream), "trace");
     cudaFree(t.trace);
@@ -829,8 +843,11 @@ int conv_tc_launch(t2sc_conv *cv, t2sc_map *m, const void *x, void *y, int flags
   a.backoff_ctl = bo_env[1];
   a.backoff_copy = bo_env[2];
   static const int wait_env = getenv("T2SC_WAIT_MODE") ? atoi(getenv("T2SC_WAIT_MODE")) : 0;
+  static const int elect_env = getenv("T2SC_WAIT_ELECT") ? atoi(getenv("T2SC_WAIT_ELECT")) : 0;
+  a.wait_elect = elect_env;
   a.wait_mode = wait_env;
   a.l1 = l1_env;
+
   a.contiguous = contig_env;
   int cols = 32;
   while (cols < 2 * cv->bn) cols <<= 1;
@@ -880,11 +897,21 @@ int conv_tc_launch(t2sc_conv *cv, t2sc_map *m, const void *x, void *y, int flags
   const int64_t slots = (int64_t)cv->ctx->num_sms * ctas;
   const int grid = (int)(nunits < slots ? nunits : slots);
   if (cv->dtype == T2SC_DT_F32) {
-    // split x into TF32 hi/lo parts in stream-ordered scratch
-    cudaStream_t st = cv->ctx->stream;
+    // split x into TF32 hi/lo parts in the context's grow-only scratch
+    // (stream-ordered: calls on the context's stream reuse it in turn; it
+    // is reallocated only when a larger input arrives)
+    t2sc_ctx *ctx = cv->ctx;
+    cudaStream_t st = ctx->stream;
     const int64_t cnt = m->n_src * (int64_t)cv->ci;
-    float *split = nullptr;
-    T2SC_CUDA(cudaMallocAsync((void **)&split, (size_t)cnt * 8, st), "split scratch");
+    const size_t need = (size_t)cnt * 8;
+    if (ctx->stage_cap[0] < need) {
+      if (ctx->stage[0]) cudaFreeAsync(ctx->stage[0], st);
+      ctx->stage[0] = nullptr;
+      ctx->stage_cap[0] = 0;
+      T2SC_CUDA(cudaMallocAsync(&ctx->stage[0], need, st), "split scratch");
+      ctx->stage_cap[0] = need;
+    }
+    float *split = static_cast<float *>(ctx->stage[0]);
     const int64_t n4 = cnt / 4;
     split_tf32_kernel<<<(unsigned)((n4 + 255) / 256), 256, 0, st>>>((const float4 *)x, (float4 *)split,
                                                                      (float4 *)(split + cnt), n4);
@@ -893,7 +920,6 @@ int conv_tc_launch(t2sc_conv *cv, t2sc_map *m, const void *x, void *y, int flags
     a.x_lo = reinterpret_cast<const uint8_t *>(split + cnt);
     int rc = cv->row_bytes == 64 ? launch_tc<kModeTf32x3, 64>(cv, a, grid, smem, err)
                                  : launch_tc<kModeTf32x3, 32>(cv, a, grid, smem, err);
-    cudaFreeAsync(split, st);
     return rc;
   }
   const bool bf = cv->dtype == T2SC_DT_BF16;

@@ -37,8 +37,13 @@ __device__ __forceinline__ uint64_t mix64(uint64_t k) {
   return k;
 }
 
-__global__ void hash_insert_kernel(const int4 *__restrict__ coords, int64_t n, unsigned long long *keys,
-                                   int32_t *vals, uint64_t hmask, int *err) {
+// Home slot of a key. (Grouping the 8 keys of a z / 8 column segment into
+// one 128-byte line was measured slower: 0.57 vs 0.41 ms for the cfg4 map,
+// longer probe runs and contended insert atomics.)
+__device__ __forceinline__ uint64_t home_slot(uint64_t key, uint64_t hmask) { return mix64(key) & hmask; }
+
+__global__ void hash_insert_kernel(const int4 *__restrict__ coords, int64_t n, longlong2 *slots, uint64_t hmask,
+                                   int *err) {
   int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (r >= n) return;
   int4 c = coords[r];
@@ -47,11 +52,12 @@ __global__ void hash_insert_kernel(const int4 *__restrict__ coords, int64_t n, u
     return;
   }
   unsigned long long key = (unsigned long long)pack_key(c.x, c.y, c.z, c.w);
-  uint64_t s = mix64(key) & hmask;
+  uint64_t s = home_slot(key, hmask);
   for (uint64_t probe = 0; probe <= hmask; probe++) {
-    unsigned long long prev = atomicCAS(&keys[s], (unsigned long long)kEmpty, key);
+    unsigned long long *kp = reinterpret_cast<unsigned long long *>(&slots[s].x);
+    unsigned long long prev = atomicCAS(kp, (unsigned long long)kEmpty, key);
     if (prev == (unsigned long long)kEmpty || prev == key) {
-      atomicMax(&vals[s], (int32_t)r);  // the last row with this key wins
+      atomicMax(reinterpret_cast<int *>(&slots[s].y), (int32_t)r);  // the last row with this key wins
       return;
     }
     s = (s + 1) & hmask;
@@ -59,14 +65,13 @@ __global__ void hash_insert_kernel(const int4 *__restrict__ coords, int64_t n, u
   atomicOr(err, kDevErrHashFull);
 }
 
-__device__ __forceinline__ int32_t hash_find(const int64_t *__restrict__ keys, const int32_t *__restrict__ vals,
-                                             uint64_t hmask, int64_t key) {
+__device__ __forceinline__ int32_t hash_find(const longlong2 *__restrict__ slots, uint64_t hmask, int64_t key) {
   if (key == kEmpty) return -1;
-  uint64_t s = mix64((uint64_t)key) & hmask;
+  uint64_t s = home_slot((uint64_t)key, hmask);
   for (uint64_t probe = 0; probe <= hmask; probe++) {
-    int64_t k = keys[s];
-    if (k == key) return vals[s];
-    if (k == kEmpty) return -1;
+    const longlong2 e = slots[s];  // key and row in one 16-byte load
+    if (e.x == key) return (int32_t)e.y;
+    if (e.x == kEmpty) return -1;
     s = (s + 1) & hmask;
   }
   return -1;
@@ -81,14 +86,15 @@ __device__ __forceinline__ void offset_of(int k, int kd, int kh, int kw, int dil
   o3 = (int64_t)(kx - kw / 2) * dil;
 }
 
-// Pass 1: occupancy mask of every target row. One warp per row, lane k
-// probes offset k, so the 27 probes of a row are in flight together; the
-// warp's ballot is the row's mask. Edges are counted per block, then
-// added once to *n_edges.
+// Pass 1: neighbours and occupancy mask of every target row. One warp per
+// row, lane k probes offset k, so the 27 probes of a row are in flight
+// together; the row's results are one 128-byte line of rows32 [n][32]; the
+// warp's ballot is the row's mask. Edges are counted per block, then added
+// once to *n_edges.
 __global__ void __launch_bounds__(256) row_mask_kernel(const int4 *__restrict__ coords, int64_t n,
-                                                       const int64_t *__restrict__ keys,
-                                                       const int32_t *__restrict__ vals, uint64_t hmask, int kd,
+                                                       const longlong2 *__restrict__ slots, uint64_t hmask, int kd,
                                                        int kh, int kw, int dil, uint32_t *__restrict__ mask,
+                                                       int32_t *__restrict__ rows32,
                                                        unsigned long long *__restrict__ n_edges) {
   __shared__ unsigned block_edges;
   if (threadIdx.x == 0) block_edges = 0;
@@ -100,9 +106,9 @@ __global__ void __launch_bounds__(256) row_mask_kernel(const int4 *__restrict__ 
   if (lane < K) offset_of(lane, kd, kh, kw, dil, o1, o2, o3);
   for (int64_t r = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); r < n; r += warps) {
     const int4 c = coords[r];
-    bool hit = false;
-    if (lane < K) hit = hash_find(keys, vals, hmask, pack_key(c.x, c.y + o1, c.z + o2, c.w + o3)) >= 0;
-    const uint32_t m = __ballot_sync(0xffffffffu, hit);
+    const int32_t src = lane < K ? hash_find(slots, hmask, pack_key(c.x, c.y + o1, c.z + o2, c.w + o3)) : -1;
+    rows32[r * 32 + lane] = src;  // one 128-byte line per row
+    const uint32_t m = __ballot_sync(0xffffffffu, src >= 0);
     if (lane == 0) {
       mask[r] = m;
       cnt += __popc(m);
@@ -114,42 +120,39 @@ __global__ void __launch_bounds__(256) row_mask_kernel(const int4 *__restrict__ 
 }
 
 // Pass 2 (after rows are sorted by mask): neighbour rows in sorted order.
-// Block (tile t, offset k) has one thread per tile row p; only offsets the
-// row's mask marks as hits are probed again, the rest are written as -1.
-// nbr_sorted[k][p] is written coalesced; the (t, 0) blocks also write the
-// padded permutation and the tile's offset mask.
-__global__ void __launch_bounds__(kTileRows) sorted_nbr_kernel(const int4 *__restrict__ coords, int64_t n,
-                                                              int64_t n_pad, const int32_t *__restrict__ sorted_rows,
+// One 128-thread block per tile: each warp reads the 128-byte result lines
+// of 32 of the tile's rows (one coalesced line per row), the block
+// transposes them in shared memory and writes nbr_sorted[k][tile rows] as
+// one 512-byte run per offset; it also writes the padded permutation and
+// the tile's offset mask.
+__global__ void __launch_bounds__(kTileRows) sorted_nbr_kernel(int64_t n, int64_t n_pad, int kvol,
+                                                              const int32_t *__restrict__ sorted_rows,
                                                               const uint32_t *__restrict__ mask,
-                                                              const int64_t *__restrict__ keys,
-                                                              const int32_t *__restrict__ vals, uint64_t hmask,
-                                                              int kd, int kh, int kw, int dil,
+                                                              const int32_t *__restrict__ rows32,
                                                               int32_t *__restrict__ perm_out,
                                                               int32_t *__restrict__ nbr_sorted,
                                                               uint32_t *__restrict__ tile_mask) {
-  const int64_t p = (int64_t)blockIdx.x * kTileRows + threadIdx.x;
-  const int k = blockIdx.y;
-  const int32_t row = p < n ? sorted_rows[p] : -1;
-  const uint32_t m = row >= 0 ? mask[row] : 0u;
-  int32_t hit = -1;
-  if ((m >> k) & 1u) {
-    int64_t o1, o2, o3;
-    offset_of(k, kd, kh, kw, dil, o1, o2, o3);
-    const int4 c = coords[row];
-    hit = hash_find(keys, vals, hmask, pack_key(c.x, c.y + o1, c.z + o2, c.w + o3));
+  __shared__ int32_t tr[32][kTileRows + 1];
+  __shared__ uint32_t wm[kTileRows / 32];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t base = (int64_t)blockIdx.x * kTileRows;
+  for (int i = 0; i < 32; i++) {
+    const int pl = warp * 32 + i;
+    const int64_t p = base + pl;
+    const int32_t row = p < n ? sorted_rows[p] : -1;
+    tr[lane][pl] = row >= 0 ? rows32[(int64_t)row * 32 + lane] : -1;
   }
-  nbr_sorted[(int64_t)k * n_pad + p] = hit;
-  if (k == 0) {
-    __shared__ uint32_t wm[kTileRows / 32];
-    perm_out[p] = row;
-    const uint32_t w = __reduce_or_sync(0xffffffffu, m);
-    if ((threadIdx.x & 31) == 0) wm[threadIdx.x >> 5] = w;
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      uint32_t t = 0;
-      for (int i = 0; i < kTileRows / 32; i++) t |= wm[i];
-      tile_mask[blockIdx.x] = t;
-    }
+  const int64_t p = base + threadIdx.x;
+  const int32_t row = p < n ? sorted_rows[p] : -1;
+  perm_out[p] = row;
+  const uint32_t m = __reduce_or_sync(0xffffffffu, row >= 0 ? mask[row] : 0u);
+  if (lane == 0) wm[warp] = m;
+  __syncthreads();
+  for (int k = 0; k < kvol; k++) nbr_sorted[(int64_t)k * n_pad + p] = tr[k][threadIdx.x];
+  if (threadIdx.x == 0) {
+    uint32_t t = 0;
+    for (int i = 0; i < kTileRows / 32; i++) t |= wm[i];
+    tile_mask[blockIdx.x] = t;
   }
 }
 
@@ -231,13 +234,11 @@ int build_hash(t2sc_coords *c, std::string &err) {
   uint64_t cap = 1024;
   while (cap < (uint64_t)(2 * c->n)) cap <<= 1;
   c->hcap = cap;
-  T2SC_CUDA(cudaMallocAsync((void **)&c->d_keys, cap * sizeof(int64_t), ctx->stream), "hash keys");
-  T2SC_CUDA(cudaMallocAsync((void **)&c->d_vals, cap * sizeof(int32_t), ctx->stream), "hash vals");
-  T2SC_CUDA(cudaMemsetAsync(c->d_keys, 0xff, cap * sizeof(int64_t), ctx->stream), "hash init");
-  T2SC_CUDA(cudaMemsetAsync(c->d_vals, 0xff, cap * sizeof(int32_t), ctx->stream), "hash init");
+  T2SC_CUDA(cudaMallocAsync((void **)&c->d_slots, cap * sizeof(longlong2), ctx->stream), "hash slots");
+  // every byte 0xff: keys and rows read as -1 (empty)
+  T2SC_CUDA(cudaMemsetAsync(c->d_slots, 0xff, cap * sizeof(longlong2), ctx->stream), "hash init");
   if (c->n > 0) {
-    hash_insert_kernel<<<nblk(c->n, 256), 256, 0, ctx->stream>>>((const int4 *)c->d_coords, c->n,
-                                                               (unsigned long long *)c->d_keys, c->d_vals,
+    hash_insert_kernel<<<nblk(c->n, 256), 256, 0, ctx->stream>>>((const int4 *)c->d_coords, c->n, c->d_slots,
                                                                cap - 1, ctx->d_err);
     T2SC_LAUNCHED(ctx, "hash_insert");
   }
@@ -325,8 +326,9 @@ int build_identity_map(t2sc_ctx *ctx, int64_t n, t2sc_map **out, std::string &er
 }
 
 // Neighbour map of a coordinate set, entirely stream-ordered (no host
-// synchronisation): row masks (one warp per row), rows sorted by mask into
-// 128-row tiles, then the neighbour rows written directly in sorted order.
+// synchronisation): neighbours and masks per row (one warp per row), rows
+// sorted by mask into 128-row tiles, then the neighbour rows transposed
+// into the sorted [K][n_pad] layout.
 int build_map(t2sc_coords *c, int kd, int kh, int kw, int dil, t2sc_map **out, std::string &err) {
   auto key = std::make_tuple(kd, kh, kw, dil);
   auto it = c->maps.find(key);
@@ -347,8 +349,10 @@ int build_map(t2sc_coords *c, int kd, int kh, int kw, int dil, t2sc_map **out, s
     const int4 *tc = (const int4 *)c->d_coords + c->target_begin;
     const int warps_per_block = 8;
     const int64_t blocks = std::min<int64_t>((n + warps_per_block - 1) / warps_per_block, (int64_t)ctx->num_sms * 64);
-    row_mask_kernel<<<(unsigned)blocks, 32 * warps_per_block, 0, st>>>(tc, n, c->d_keys, c->d_vals, c->hcap - 1, kd,
-                                                                       kh, kw, dil, m->mask, m->d_edges);
+    int32_t *rows32 = nullptr;
+    T2SC_CUDA(cudaMallocAsync((void **)&rows32, sizeof(int32_t) * 32 * n, st), "map scratch");
+    row_mask_kernel<<<(unsigned)blocks, 32 * warps_per_block, 0, st>>>(tc, n, c->d_slots, c->hcap - 1, kd, kh, kw,
+                                                                       dil, m->mask, rows32, m->d_edges);
     T2SC_LAUNCHED(ctx, "row_mask");
     int32_t *iota = nullptr, *sorted = nullptr;
     void *temp = nullptr;
@@ -390,10 +394,10 @@ int build_map(t2sc_coords *c, int kd, int kh, int kw, int dil, t2sc_map **out, s
       cudaFreeAsync(keys, st);
       cudaFreeAsync(keys_sorted, st);
     }
-    sorted_nbr_kernel<<<dim3((unsigned)m->ntiles, (unsigned)K), kTileRows, 0, st>>>(
-        tc, n, m->n_pad, sorted, m->mask, c->d_keys, c->d_vals, c->hcap - 1, kd, kh, kw, dil, m->perm,
-        m->nbr_sorted, m->tile_mask);
+    sorted_nbr_kernel<<<(unsigned)m->ntiles, kTileRows, 0, st>>>(n, m->n_pad, K, sorted, m->mask, rows32, m->perm,
+                                                                 m->nbr_sorted, m->tile_mask);
     T2SC_LAUNCHED(ctx, "sorted_nbr");
+    cudaFreeAsync(rows32, st);
     if (temp) cudaFreeAsync(temp, st);
     cudaFreeAsync(sorted, st);
     cudaFreeAsync(iota, st);

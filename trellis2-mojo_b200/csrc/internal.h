@@ -39,6 +39,8 @@ struct Status {
 
 }  // namespace t2sc
 
+struct t2sc_map;
+
 struct t2sc_ctx {
   int device = 0;
   int num_sms = 148;
@@ -49,7 +51,10 @@ struct t2sc_ctx {
   int tile_order = 0;        // TileOrder of the conv maps built on this context
   int64_t tile_chunk = 1024; // rows per run for kOrderChunked
   std::string last_error;
-  // grow-only staging buffers for the host-pointer entry points
+  // identity row maps of the linear layers, one per row count, shared by
+  // every linear handle of the context and kept until it is destroyed
+  std::map<int64_t, t2sc_map *> id_maps;
+  // grow-only scratch buffers ([0]: the split-TF32 hi/lo parts of a conv input)
   void *stage[4] = {nullptr, nullptr, nullptr, nullptr};
   size_t stage_cap[4] = {0, 0, 0, 0};
 };
@@ -77,8 +82,9 @@ struct t2sc_coords {
   int64_t target_begin = 0;      // first target row (targets are rows [target_begin, +n_targets))
   int32_t *d_coords = nullptr;   // [n,4]
   uint64_t hcap = 0;             // hash capacity (power of two)
-  int64_t *d_keys = nullptr;     // [hcap]
-  int32_t *d_vals = nullptr;     // [hcap]
+  // [hcap] slots of 16 bytes: int64 key, int32 row, 4 bytes padding (a
+  // probe reads key and row with one load)
+  longlong2 *d_slots = nullptr;
   std::map<std::tuple<int, int, int, int>, t2sc_map *> maps;
 };
 
@@ -94,7 +100,6 @@ struct t2sc_conv {
   int tc_path = 0;               // 1 = tcgen05 path, 0 = SIMT path
   float *d_w_simt = nullptr;     // [K][ci][co] f32 (SIMT path)
   void *d_w_lo = nullptr;        // split-TF32 low parts image (f32 mode)
-  t2sc_map *lin_map = nullptr;   // identity map of the last row count (linear layers)
 };
 
 namespace t2sc {

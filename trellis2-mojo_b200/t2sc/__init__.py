@@ -8,5 +8,6 @@ from .sparse import (Binarized, Context, LayerNorm32, Coords, SparseChannel2Spat
                      SparseResBlockC2S3d, SparseTensor,
                      SparseUpsample, binarize, conv_chain, sparse_conv3d_from)
 from . import synth  # noqa: F401
+from .decoder import SparseConvNeXtBlock3d, SparseUnetVaeDecoder  # noqa: F401
 
 __version__ = "0.1"

@@ -53,6 +53,9 @@ SIGNATURES = {
     "t2sc_linear_create": (I32, [P, P, P, I32, I32, I32, PP]),
     "t2sc_linear_forward_device": (I32, [P, P, P, I64, I32, P]),
     "t2sc_layernorm_device": (I32, [P, P, P, I64, I32, P, P, F, I32, I32]),
+    "t2sc_convnext_block_create": (I32, [P, I32, I32, P, P, P, P, P, P, P, P, I32, PP]),
+    "t2sc_convnext_block_destroy": (I32, [P]),
+    "t2sc_convnext_block_forward_device": (I32, [P, P, P, P]),
     "t2sc_c2s_block_create": (I32, [P, I32, I32, I32, P, P, P, P, P, P, P, P, I32, PP]),
     "t2sc_c2s_block_destroy": (I32, [P]),
     "t2sc_c2s_block_forward_device": (I32, [P, P, P, P, P, P, PI64, PP]),

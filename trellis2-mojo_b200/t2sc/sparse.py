@@ -95,6 +95,16 @@ class Coords:
         check(lib.t2sc_coords_count(h, ctypes.byref(v)))
         self.n = v.value
 
+    @classmethod
+    def from_handle(cls, ctx, handle):
+        """Wraps a coordinate handle the library returned (owned from now on)."""
+        self = cls.__new__(cls)
+        self.ctx, self.handle = ctx, handle
+        v = ctypes.c_int64()
+        check(lib.t2sc_coords_count(handle, ctypes.byref(v)))
+        self.n = v.value
+        return self
+
     def build_map(self, kernel=(3, 3, 3), dilation=1):
         e = ctypes.c_int64()
         check(lib.t2sc_coords_build_map(self.handle, *kernel, dilation, ctypes.byref(e)), self.ctx.handle)
