@@ -43,6 +43,7 @@
 #include <cuda_fp16.h>
 
 #include "internal.h"
+#include "epilogue.cuh"
 #include "sm100.cuh"
 
 #ifndef T2SC_CONV_DIAGNOSTICS
@@ -66,18 +67,35 @@ constexpr int kSmemHalf = 115712;  // per block when two share an SM's 228 KB (1
 #define T2SC_CTAS_PER_SM 2
 #endif
 constexpr int kDefaultCtasPerSm = T2SC_CTAS_PER_SM;
-constexpr int kModeTf32x3 = 3;    // beside T2SC_DT_F16 (1) and T2SC_DT_BF16 (2)
+constexpr int kModeTf32x3 = kEpiF32;  // beside T2SC_DT_F16 (1) and T2SC_DT_BF16 (2)
 constexpr int kCopyWarp0 = 4;
-// Warp roles: 0-3 epilogue; kCopyWarps copy warps (8 in the 16-bit modes,
-// 4 in the split-TF32 mode, whose epilogue needs the registers); one
-// control warp (weight copies, index prefetch); one MMA warp.
+// Warp roles: 0-3 epilogue (warp q reads TMEM lane quadrant q); kCopyWarps
+// copy warps (8 in the 16-bit modes, 4 in the split-TF32 mode, whose
+// epilogue needs the registers); one control warp (weight copies, index
+// prefetch); one MMA warp.
+//
+// A warp issues from scheduler (SM sub-partition) warp % 4. The MMA warp
+// issues every tcgen05.mma of the CTA from one thread and the conv runs at
+// that thread's pace, so in the 16-bit modes (SPLIT layout) it sits on
+// sub-partition 1 with only the quadrant-1 epilogue warp (idle most of the
+// time), the control warp on 3 and the copy warps on 0, 2 and 3:
+//   warp  0 1 2 3 | 4 5   6 7 | 8 9    10 11 | 12 13   14 15
+//   role  E E E E | C MMA C C | C idle C  C  | C  idle C  control
+// 16 warps keep the pattern for a second CTA on the SM.
 template <int DT, int RB = 128>
 struct Roles {
+  static constexpr bool kSplitLayout = DT != 3;
   // 16-byte vectors per row: each warp must own >= 32 / (RB / 16) rows
-  static constexpr int kCopyWarps = DT == 3 ? 4 : (RB == 128 ? T2SC_COPY_WARPS_128 : 8);
-  static constexpr int kControlWarp = kCopyWarp0 + kCopyWarps;
-  static constexpr int kMmaWarp = kControlWarp + 1;
-  static constexpr int kThreads = 32 * (kMmaWarp + 1);
+  static constexpr int kCopyWarps = DT == 3 ? 4 : 8;
+  static constexpr int kControlWarp = kSplitLayout ? 15 : kCopyWarp0 + kCopyWarps;
+  static constexpr int kMmaWarp = kSplitLayout ? 5 : kControlWarp + 1;
+  static constexpr int kThreads = kSplitLayout ? 512 : 32 * (kMmaWarp + 1);
+  // copy-warp index of warp w, or -1
+  __device__ __forceinline__ static constexpr int copy_index(int w) {
+    return kSplitLayout ? (w == 4 ? 0 : w == 6 ? 1 : w == 7 ? 2 : w == 8 ? 3 : w == 10 ? 4 : w == 11 ? 5
+                                                                 : w == 12 ? 6 : w == 14 ? 7 : -1)
+                        : (w >= kCopyWarp0 && w < kCopyWarp0 + kCopyWarps ? w - kCopyWarp0 : -1);
+  }
 };
 
 struct TcArgs {
@@ -92,6 +110,10 @@ struct TcArgs {
   const uint32_t *tile_mask; // [ntiles]
   int64_t n_pad;
   int ntiles, ci, co, bn, nchunks, nco_tiles, kvol, stages, flags, tmem_cols;
+  // independent TMEM accumulators per tile (16-bit modes): consecutive MMA
+  // k-steps go to different ones, so no MMA waits on the previous one's
+  // result; the epilogue adds them
+  int nacc;
   uint32_t a_bytes, b_bytes, sub_bytes, stage_bytes;  // per (k, chunk) pair: A, B; pair slot; stage
   int group;                                          // (k, chunk) pairs per pipeline stage
 #if T2SC_CONV_DIAGNOSTICS
@@ -120,86 +142,6 @@ constexpr int kTraceN = 4096;
   } while (0)
 #define T2SC_SKIP(bit) false
 #endif
-
-template <int DT>
-__device__ __forceinline__ uint32_t pack2(float a, float b) {
-  if (DT == T2SC_DT_BF16) {
-    __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
-    return *reinterpret_cast<uint32_t *>(&h);
-  } else {
-    __half2 h = __floats2half2_rn(a, b);
-    return *reinterpret_cast<uint32_t *>(&h);
-  }
-}
-template <int DT>
-__device__ __forceinline__ float2 unpack2(uint32_t v) {
-  if (DT == T2SC_DT_BF16) {
-    __nv_bfloat162 h = *reinterpret_cast<__nv_bfloat162 *>(&v);
-    return __bfloat1622float2(h);
-  } else {
-    __half2 h = *reinterpret_cast<__half2 *>(&v);
-    return __half22float2(h);
-  }
-}
-
-// v / (1 + exp(-v)); the exponent is clamped so the divisor stays in the
-// range where the fast division is accurate (SiLU(v) for v < -80 is below
-// 1e-33 either way).
-__device__ __forceinline__ float silu(float v) { return __fdividef(v, 1.0f + __expf(fminf(-v, 80.0f))); }
-
-// Epilogue for 16 consecutive output channels of one row.
-template <int DT>
-__device__ __forceinline__ void store16(const TcArgs &a, int orow, int col, const float (&acc)[16]) {
-  float v[16];
-#pragma unroll
-  for (int i = 0; i < 16; i++) v[i] = acc[i] + __ldg(a.bias + col + i);
-  if (a.flags & T2SC_SILU) {
-#pragma unroll
-    for (int i = 0; i < 16; i++) v[i] = silu(v[i]);
-  }
-  if (DT == kModeTf32x3) {
-    const int64_t off = ((int64_t)orow * a.co + col) * 4;
-    if (a.flags & T2SC_RESIDUAL) {
-      const float4 *rp = reinterpret_cast<const float4 *>(a.res + off);
-#pragma unroll
-      for (int q = 0; q < 4; q++) {
-        float4 r = __ldg(rp + q);
-        v[4 * q] += r.x;
-        v[4 * q + 1] += r.y;
-        v[4 * q + 2] += r.z;
-        v[4 * q + 3] += r.w;
-      }
-    }
-    float4 *yp = reinterpret_cast<float4 *>(a.y + off);
-#pragma unroll
-    for (int q = 0; q < 4; q++) yp[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
-    return;
-  }
-  const int64_t off = ((int64_t)orow * a.co + col) * 2;
-  if (a.flags & T2SC_RESIDUAL) {
-    const uint4 *rp = reinterpret_cast<const uint4 *>(a.res + off);
-    uint4 r0 = __ldg(rp), r1 = __ldg(rp + 1);
-    uint32_t rr[8] = {r0.x, r0.y, r0.z, r0.w, r1.x, r1.y, r1.z, r1.w};
-#pragma unroll
-    for (int i = 0; i < 8; i++) {
-      float2 f = unpack2<DT>(rr[i]);
-      v[2 * i] += f.x;
-      v[2 * i + 1] += f.y;
-    }
-  }
-  uint4 o0, o1;
-  o0.x = pack2<DT>(v[0], v[1]);
-  o0.y = pack2<DT>(v[2], v[3]);
-  o0.z = pack2<DT>(v[4], v[5]);
-  o0.w = pack2<DT>(v[6], v[7]);
-  o1.x = pack2<DT>(v[8], v[9]);
-  o1.y = pack2<DT>(v[10], v[11]);
-  o1.z = pack2<DT>(v[12], v[13]);
-  o1.w = pack2<DT>(v[14], v[15]);
-  uint4 *yp = reinterpret_cast<uint4 *>(a.y + off);
-  yp[0] = o0;
-  yp[1] = o1;
-}
 
 // Warp-uniform bounded wait. Every lane probes the barrier (the common
 // case, an already completed phase, costs one probe). Otherwise lane 0
@@ -252,8 +194,10 @@ __device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, volatil
   return __all_sync(0xffffffffu, ok);
 }
 
-template <int DT, int RB>
-__global__ void __launch_bounds__(Roles<DT, RB>::kThreads, 1)
+// NA: independent accumulators per tile (a.nacc, fixed at compile time so
+// the MMA thread spends no instructions choosing them).
+template <int DT, int RB, int NA>
+__global__ void __launch_bounds__(Roles<DT, RB>::kThreads, Roles<DT, RB>::kSplitLayout ? 2 : 1)
     conv_tc_kernel(const TcArgs a) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // 1024-byte alignment for the swizzle atoms
@@ -315,7 +259,8 @@ __global__ void __launch_bounds__(Roles<DT, RB>::kThreads, 1)
 
   // tile masks are read ahead so no global-load latency sits at a unit boundary
   auto mask_of = [&](int unit) -> uint32_t { return unit < nunits ? __ldg(a.tile_mask + unit / a.nco_tiles) : 0u; };
-  if (warp >= kCopyWarp0 && warp < kControlWarp) {
+  const int cw = Roles<DT, RB>::copy_index(warp);
+  if (cw >= 0) {
     // ----------------------------- copy warps -----------------------------
     // All copy warps fill every stage together: warp w owns tile rows
     // [w*RW, (w+1)*RW). Lane (rsub, j) copies 16-byte vector j of rows
@@ -327,7 +272,6 @@ __global__ void __launch_bounds__(Roles<DT, RB>::kThreads, 1)
     constexpr int RW = kTileRows / kW;    // rows per warp
     constexpr int RPL = RW * CPR / 32;    // rows per lane
     constexpr int EPV = 16 / ES;          // elements per vector
-    const int cw = warp - kCopyWarp0;
     const int j = lane % CPR, rsub = lane / CPR;
     const int row0 = cw * RW + rsub * RPL;
     uint32_t soff[RPL];
@@ -352,12 +296,12 @@ __global__ void __launch_bounds__(Roles<DT, RB>::kThreads, 1)
       const uint8_t *gp[RPL];
       uint32_t gs[RPL];
       for (int q = 0; q < npairs && ok;) {
-        if (tid == 32 * kCopyWarp0) T2SC_TRACE(0, cit);
+        if (cw == 0 && lane == 0) T2SC_TRACE(0, cit);
         if (!warp_wait(empty0 + 8 * s, ph ^ 1, abort, a.err, a.backoff_copy, a.wait_mode, a.wait_elect)) {
           ok = false;
           break;
         }
-        if (tid == 32 * kCopyWarp0) T2SC_TRACE(1, cit);
+        if (cw == 0 && lane == 0) T2SC_TRACE(1, cit);
         const uint32_t abase = sbase + s * a.stage_bytes, bar = full0 + 8 * s;
         const int valid = npairs - q < G ? npairs - q : G;
         for (int g = 0; g < valid; g++, q++) {
@@ -384,7 +328,7 @@ __global__ void __launch_bounds__(Roles<DT, RB>::kThreads, 1)
               gs[p] = src[p] >= 0 ? 16u : 0u;
             }
           }
-          if (tid == 32 * kCopyWarp0) T2SC_TRACE(10, cit);
+          if (cw == 0 && lane == 0) T2SC_TRACE(10, cit);
           const uint32_t sub = abase + g * a.sub_bytes;
           const bool cvalid = c * BKE + j * EPV < a.ci;
 #pragma unroll
@@ -400,10 +344,10 @@ __global__ void __launch_bounds__(Roles<DT, RB>::kThreads, 1)
             }
           }
         }
-        if (tid == 32 * kCopyWarp0) T2SC_TRACE(11, cit);
+        if (cw == 0 && lane == 0) T2SC_TRACE(11, cit);
         // arrives on the stage barrier once this lane's copies have landed
         sm100::cp_async_arrive_noinc(bar);
-        if (tid == 32 * kCopyWarp0) T2SC_TRACE(6, cit);
+        if (cw == 0 && lane == 0) T2SC_TRACE(6, cit);
         cit++;
         if (++s == (uint32_t)S) {
           s = 0;
@@ -575,7 +519,8 @@ __global__ void __launch_bounds__(Roles<DT, RB>::kThreads, 1)
       if (!warp_wait(tfull0 + 8 * b, (acc_it >> 1) & 1, abort, a.err, a.backoff_epi, a.wait_mode, a.wait_elect)) break;
       if (tid == 0) T2SC_TRACE(5, acc_it);
       sm100::tc_fence_after();
-      const uint32_t tbase = tmem + ((uint32_t)(32 * q) << 16) + b * a.bn;
+      const uint32_t tbase = tmem + ((uint32_t)(32 * q) << 16) + b * NA * a.bn;
+      constexpr int used = NA;  // every unit with work has >= RB / 32 >= NA k-steps
       for (int cc = 0; cc < a.bn; cc += 16) {
         uint32_t r[16];
         sm100::tmem_ld16(tbase + cc, r);
@@ -583,6 +528,12 @@ __global__ void __launch_bounds__(Roles<DT, RB>::kThreads, 1)
         float acc[16];
 #pragma unroll
         for (int i = 0; i < 16; i++) acc[i] = __uint_as_float(r[i]);
+        for (int j = 1; j < used; j++) {
+          sm100::tmem_ld16(tbase + j * a.bn + cc, r);
+          sm100::tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 16; i++) acc[i] += __uint_as_float(r[i]);
+        }
         if (orow >= 0 && !T2SC_SKIP(4)) store16<DT>(a, orow, col0 + cc, acc);
       }
       sm100::tc_fence_before();
@@ -590,7 +541,7 @@ __global__ void __launch_bounds__(Roles<DT, RB>::kThreads, 1)
       if (lane == 0) sm100::mbar_arrive(tempty0 + 8 * b);
       acc_it++;
     }
-  } else {
+  } else if (warp == kMmaWarp) {
     // ----------------------------- MMA issuer -----------------------------
     if (lane == 0) {
       const uint32_t idesc =
@@ -617,8 +568,11 @@ __global__ void __launch_bounds__(Roles<DT, RB>::kThreads, 1)
             break;
           }
           sm100::tc_fence_after();
-          const uint32_t dtm = tmem + b * a.bn;
-          uint32_t accum = 0;
+          const uint32_t dtm = tmem + b * NA * a.bn;
+          uint32_t accum = 0;  // whether the accumulators hold data (the unit's first pair sets them)
+          uint32_t dacc[NA];   // the accumulators' TMEM addresses
+#pragma unroll
+          for (int j = 0; j < NA; j++) dacc[j] = dtm + j * a.bn;
           for (int q = 0; q < pairs_per_group; q += a.group) {
             T2SC_TRACE(2, mit);
             if (!sm100::mbar_wait_bounded(full0 + 8 * s, ph, abort, a.err, kDevErrTimeout, kWaitLimit, a.wait_mode)) {
@@ -640,10 +594,13 @@ __global__ void __launch_bounds__(Roles<DT, RB>::kThreads, 1)
                   sm100::mma_tf32(dtm, ahi, blo, idesc, 1u);
                   sm100::mma_tf32(dtm, ahi, bhi, idesc, 1u);
                 } else {
-                  sm100::mma_f16(dtm, ahi, bhi, idesc, accum);
+                  // k-step kk of every pair goes to accumulator kk % nacc
+                  // (nacc divides RB / 32), cleared by the unit's first pair
+                  sm100::mma_f16(dacc[kk % NA], ahi, bhi, idesc, kk >= NA ? 1u : accum);
                 }
-                accum = 1;
+                if (kSplit) accum = 1;
               }
+              accum = 1;
             }
             sm100::mma_commit(empty0 + 8 * s);
             T2SC_TRACE(3, mit);
@@ -690,9 +647,9 @@ __global__ void split_tf32_kernel(const float4 *__restrict__ x, float4 *__restri
   lo[i] = l;
 }
 
-template <int DT, int RB>
+template <int DT, int RB, int NA>
 int launch_tc(t2sc_conv *cv, const TcArgs &args, int grid, size_t smem, std::string &err) {
-  auto kfn = conv_tc_kernel<DT, RB>;
+  auto kfn = conv_tc_kernel<DT, RB, NA>;
   // set the shared-memory opt-in once per instantiation and size (a host-only
   // call kept out of the per-launch path, e.g. during stream capture)
   static int attr_smem[64] = {};
@@ -849,8 +806,13 @@ int conv_tc_launch(t2sc_conv *cv, t2sc_map *m, const void *x, void *y, int flags
   a.l1 = l1_env;
 
   a.contiguous = contig_env;
+  // independent accumulators: up to the k-steps of a pair (RB / 32), within
+  // the SM's 512 TMEM columns (double-buffered, bn columns each)
+  static const int nacc_env = getenv("T2SC_CONV_NACC") ? atoi(getenv("T2SC_CONV_NACC")) : 4;
+  a.nacc = cv->dtype == T2SC_DT_F32 ? 1 : (nacc_env >= 4 ? 4 : nacc_env >= 2 ? 2 : 1);
+  while (a.nacc > 1 && (2 * a.nacc * cv->bn > 512 || a.nacc > cv->row_bytes / 32)) a.nacc >>= 1;
   int cols = 32;
-  while (cols < 2 * cv->bn) cols <<= 1;
+  while (cols < 2 * a.nacc * cv->bn) cols <<= 1;
   a.tmem_cols = cols;
   const int na = cv->dtype == T2SC_DT_F32 ? 2 : 1;
   a.a_bytes = kTileRows * cv->row_bytes * na;
@@ -918,21 +880,30 @@ int conv_tc_launch(t2sc_conv *cv, t2sc_map *m, const void *x, void *y, int flags
     T2SC_LAUNCHED(cv->ctx, "split_tf32");
     a.x = reinterpret_cast<const uint8_t *>(split);
     a.x_lo = reinterpret_cast<const uint8_t *>(split + cnt);
-    int rc = cv->row_bytes == 64 ? launch_tc<kModeTf32x3, 64>(cv, a, grid, smem, err)
-                                 : launch_tc<kModeTf32x3, 32>(cv, a, grid, smem, err);
+    int rc = cv->row_bytes == 64 ? launch_tc<kModeTf32x3, 64, 1>(cv, a, grid, smem, err)
+                                 : launch_tc<kModeTf32x3, 32, 1>(cv, a, grid, smem, err);
     return rc;
   }
   const bool bf = cv->dtype == T2SC_DT_BF16;
   switch (cv->row_bytes) {
     case 128:
-      return bf ? launch_tc<T2SC_DT_BF16, 128>(cv, a, grid, smem, err)
-                : launch_tc<T2SC_DT_F16, 128>(cv, a, grid, smem, err);
+      if (a.nacc == 4)
+        return bf ? launch_tc<T2SC_DT_BF16, 128, 4>(cv, a, grid, smem, err)
+                  : launch_tc<T2SC_DT_F16, 128, 4>(cv, a, grid, smem, err);
+      if (a.nacc == 2)
+        return bf ? launch_tc<T2SC_DT_BF16, 128, 2>(cv, a, grid, smem, err)
+                  : launch_tc<T2SC_DT_F16, 128, 2>(cv, a, grid, smem, err);
+      return bf ? launch_tc<T2SC_DT_BF16, 128, 1>(cv, a, grid, smem, err)
+                : launch_tc<T2SC_DT_F16, 128, 1>(cv, a, grid, smem, err);
     case 64:
-      return bf ? launch_tc<T2SC_DT_BF16, 64>(cv, a, grid, smem, err)
-                : launch_tc<T2SC_DT_F16, 64>(cv, a, grid, smem, err);
+      if (a.nacc == 2)
+        return bf ? launch_tc<T2SC_DT_BF16, 64, 2>(cv, a, grid, smem, err)
+                  : launch_tc<T2SC_DT_F16, 64, 2>(cv, a, grid, smem, err);
+      return bf ? launch_tc<T2SC_DT_BF16, 64, 1>(cv, a, grid, smem, err)
+                : launch_tc<T2SC_DT_F16, 64, 1>(cv, a, grid, smem, err);
     default:
-      return bf ? launch_tc<T2SC_DT_BF16, 32>(cv, a, grid, smem, err)
-                : launch_tc<T2SC_DT_F16, 32>(cv, a, grid, smem, err);
+      return bf ? launch_tc<T2SC_DT_BF16, 32, 1>(cv, a, grid, smem, err)
+                : launch_tc<T2SC_DT_F16, 32, 1>(cv, a, grid, smem, err);
   }
 }
 

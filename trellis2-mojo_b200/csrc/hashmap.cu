@@ -156,6 +156,103 @@ __global__ void __launch_bounds__(kTileRows) sorted_nbr_kernel(int64_t n, int64_
   }
 }
 
+// Staged-window layout of one 128-row natural-order tile (one block of 256
+// threads). The tile's (row, offset) sources, read as 32-entry lines of
+// rows32, are sorted with their entry ids in shared memory (bitonic, 4096
+// 64-bit keys src << 12 | entry); distinct sources get consecutive window
+// slots in ascending row order, and a run starts wherever a source is not
+// its predecessor + 1. Writes each entry's slot, the run list and sizes,
+// the tile's offset mask, and flags a tile that exceeds the capacities.
+__global__ void __launch_bounds__(256) win_build_kernel(const int32_t *__restrict__ rows32,
+                                                       const uint32_t *__restrict__ mask, int64_t n, int kvol,
+                                                       int16_t *__restrict__ slot16, int32_t *__restrict__ runs,
+                                                       int32_t *__restrict__ meta, uint32_t *__restrict__ tmask,
+                                                       int *__restrict__ over) {
+  constexpr int NE = kTileRows * 32;  // entries of a tile (row, lane)
+  __shared__ unsigned long long key[NE];
+  __shared__ int2 part[256];
+  const int tid = threadIdx.x;
+  const int64_t base = (int64_t)blockIdx.x * kTileRows;
+  for (int e = tid; e < NE; e += 256) {
+    const int64_t r = base + (e >> 5);
+    const int32_t src = r < n ? rows32[r * 32 + (e & 31)] : -1;
+    key[e] = src >= 0 ? ((unsigned long long)src << 12) | (unsigned)e : ~0ull;
+  }
+  __syncthreads();
+  for (int k = 2; k <= NE; k <<= 1)
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      for (int i = tid; i < NE; i += 256) {
+        const int ixj = i ^ j;
+        if (ixj > i) {
+          const unsigned long long a = key[i], b = key[ixj];
+          if ((a > b) == ((i & k) == 0)) key[i] = b, key[ixj] = a;
+        }
+      }
+      __syncthreads();
+    }
+  // flags per entry: first of its source (a new slot), first of a run
+  constexpr int PER = NE / 256;
+  int ns[PER], nr[PER];
+  int2 sum = make_int2(0, 0);
+  for (int q = 0; q < PER; q++) {
+    const int i = tid * PER + q;
+    const unsigned long long kv = key[i];
+    const bool valid = kv != ~0ull;
+    const long long src = (long long)(kv >> 12);
+    const long long prev = i > 0 && key[i - 1] != ~0ull ? (long long)(key[i - 1] >> 12) : -2;
+    ns[q] = valid && src != prev;
+    nr[q] = ns[q] && src != prev + 1;
+    sum.x += ns[q];
+    sum.y += nr[q];
+  }
+  part[tid] = sum;
+  __syncthreads();
+  if (tid < 32) {  // exclusive scan of the 256 partial sums by one warp
+    int2 v[8], run = make_int2(0, 0);
+    for (int q = 0; q < 8; q++) v[q] = part[tid * 8 + q], run.x += v[q].x, run.y += v[q].y;
+    int2 incl = run;
+    for (int d = 1; d < 32; d <<= 1) {
+      const int ax = __shfl_up_sync(0xffffffffu, incl.x, d), ay = __shfl_up_sync(0xffffffffu, incl.y, d);
+      if (tid >= d) incl.x += ax, incl.y += ay;
+    }
+    int2 acc = make_int2(incl.x - run.x, incl.y - run.y);
+    for (int q = 0; q < 8; q++) {
+      const int2 t = v[q];
+      part[tid * 8 + q] = acc;
+      acc.x += t.x, acc.y += t.y;
+    }
+    if (tid == 31) {
+      meta[blockIdx.x * 2] = incl.y;      // runs
+      meta[blockIdx.x * 2 + 1] = incl.x;  // window rows
+      if (incl.x > kWinRows || incl.y > kWinRunCap) atomicOr(over, 1);
+    }
+  }
+  __syncthreads();
+  int2 acc = part[tid];
+  for (int q = 0; q < PER; q++) {
+    const int i = tid * PER + q;
+    acc.x += ns[q];
+    acc.y += nr[q];
+    const unsigned long long kv = key[i];
+    if (kv == ~0ull) continue;
+    const int slot = acc.x - 1, e = (int)(kv & 4095u);
+    if (slot < kWinRows && (e & 31) < kvol)
+      slot16[((int64_t)blockIdx.x * kvol + (e & 31)) * kTileRows + (e >> 5)] = (int16_t)slot;
+    if (nr[q] && acc.y - 1 < kWinRunCap) {
+      int32_t *rp = runs + ((int64_t)blockIdx.x * kWinRunCap + acc.y - 1) * 2;
+      rp[0] = (int32_t)(kv >> 12);
+      rp[1] = slot;
+    }
+  }
+  if (tid < 32) {
+    uint32_t m = 0;
+    for (int p = tid; p < kTileRows; p += 32)
+      if (base + p < n) m |= mask[base + p];
+    m = __reduce_or_sync(0xffffffffu, m);
+    if (tid == 0) tmask[blockIdx.x] = m;
+  }
+}
+
 // pos[perm[p]] = p: sorted position of every target row (for the exports,
 // which list edges in the reference's row order).
 __global__ void inverse_perm_kernel(const int32_t *__restrict__ perm, int64_t n_pad, int32_t *__restrict__ pos) {
@@ -264,6 +361,11 @@ void free_map(t2sc_map *m) {
   cudaFreeAsync(m->perm, st);
   cudaFreeAsync(m->nbr_sorted, st);
   cudaFreeAsync(m->tile_mask, st);
+  if (m->slot16) cudaFreeAsync(m->slot16, st);
+  if (m->win_runs) cudaFreeAsync(m->win_runs, st);
+  if (m->win_meta) cudaFreeAsync(m->win_meta, st);
+  if (m->tile_mask_nat) cudaFreeAsync(m->tile_mask_nat, st);
+  if (m->d_win_over) cudaFreeAsync(m->d_win_over, st);
   delete m;
 }
 
@@ -277,6 +379,17 @@ int map_edges(t2sc_map *m, int64_t *n_edges, std::string &err) {
     m->n_edges = (int64_t)e;
   }
   *n_edges = m->n_edges;
+  return T2SC_OK;
+}
+
+int map_win_ok(t2sc_map *m, int *ok, std::string &err) {
+  if (m->win_ok < 0) {
+    int over = 1;
+    T2SC_CUDA(cudaMemcpyAsync(&over, m->d_win_over, sizeof(int), cudaMemcpyDeviceToHost, m->ctx->stream), "win flag");
+    T2SC_CUDA(cudaStreamSynchronize(m->ctx->stream), "win flag");
+    m->win_ok = over ? 0 : 1;
+  }
+  *ok = m->win_ok;
   return T2SC_OK;
 }
 
@@ -397,6 +510,20 @@ int build_map(t2sc_coords *c, int kd, int kh, int kw, int dil, t2sc_map **out, s
     sorted_nbr_kernel<<<(unsigned)m->ntiles, kTileRows, 0, st>>>(n, m->n_pad, K, sorted, m->mask, rows32, m->perm,
                                                                  m->nbr_sorted, m->tile_mask);
     T2SC_LAUNCHED(ctx, "sorted_nbr");
+    if (ctx->conv_win) {  // staged-window layout for conv_win.cu
+      const size_t nt = (size_t)m->ntiles;
+      T2SC_CUDA(cudaMallocAsync((void **)&m->slot16, sizeof(int16_t) * K * (size_t)m->n_pad, st), "win map");
+      T2SC_CUDA(cudaMallocAsync((void **)&m->win_runs, sizeof(int32_t) * 2 * kWinRunCap * nt, st), "win map");
+      T2SC_CUDA(cudaMallocAsync((void **)&m->win_meta, sizeof(int32_t) * 2 * nt, st), "win map");
+      T2SC_CUDA(cudaMallocAsync((void **)&m->tile_mask_nat, sizeof(uint32_t) * nt, st), "win map");
+      T2SC_CUDA(cudaMallocAsync((void **)&m->d_win_over, sizeof(int), st), "win map");
+      T2SC_CUDA(cudaMemsetAsync(m->slot16, 0xff, sizeof(int16_t) * K * (size_t)m->n_pad, st), "win map");
+      T2SC_CUDA(cudaMemsetAsync(m->d_win_over, 0, sizeof(int), st), "win map");
+      win_build_kernel<<<(unsigned)nt, 256, 0, st>>>(rows32, m->mask, n, K, m->slot16, m->win_runs,
+                                                     m->win_meta, m->tile_mask_nat, m->d_win_over);
+      T2SC_LAUNCHED(ctx, "win_build");
+      m->win_ok = -1;
+    }
     cudaFreeAsync(rows32, st);
     if (temp) cudaFreeAsync(temp, st);
     cudaFreeAsync(sorted, st);
