@@ -116,11 +116,6 @@ int t2sc_ctx_create(int device, t2sc_ctx **out) {
       cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep);
     }
     ctx->stream = ctx->own_stream;
-    // tuning knobs (tile grouping only; results do not depend on them)
-    if (const char *e = getenv("T2SC_TILE_ORDER")) ctx->tile_order = atoi(e);
-    if (const char *e = getenv("T2SC_TILE_CHUNK")) ctx->tile_chunk = atoll(e);
-    if (const char *e = getenv("T2SC_CONV_WIN")) ctx->conv_win = atoi(e) != 0;
-    if (ctx->tile_order < 0 || ctx->tile_order > 2) ctx->tile_order = 0;
     if (cudaMalloc((void **)&ctx->d_err, sizeof(int)) != cudaSuccess) return T2SC_ERR_OOM;
     if (cudaMemset(ctx->d_err, 0, sizeof(int)) != cudaSuccess) return T2SC_ERR_CUDA;
     *out = ctx.release();
@@ -353,10 +348,6 @@ static int forward_device_impl(t2sc_conv *cv, t2sc_coords *c, const void *x, voi
   if (c->n > 0 && (!x || !y)) return fail(ctx, T2SC_ERR_INVALID, "null feature buffer");
   t2sc_map *m = nullptr;
   T2SC_TRY(build_map(c, cv->kd, cv->kh, cv->kw, cv->dilation, &m, ctx->last_error));
-  if (ctx->conv_win && cv->tc_path) {  // the staged-window kernel where it applies
-    const int rc = conv_win_launch(cv, m, x, y, flags, residual, ctx->last_error);
-    if (rc != T2SC_ERR_UNSUPPORTED) return rc;
-  }
   return cv->tc_path ? conv_tc_launch(cv, m, x, y, flags, residual, ctx->last_error)
                      : conv_simt_launch(cv, m, x, y, flags, residual, ctx->last_error);
 }

@@ -50,8 +50,10 @@
 #define T2SC_CONV_DIAGNOSTICS 0
 #endif
 
-#ifndef T2SC_COPY_WARPS_128
-#define T2SC_COPY_WARPS_128 8
+// copy warps per CTA in the 16-bit modes: 4 measured ~10 % faster than 8 at
+// the 512^3 decoder level (0.130 vs 0.145 ms per layer)
+#ifndef T2SC_COPY_WARPS
+#define T2SC_COPY_WARPS 4
 #endif
 
 namespace t2sc {
@@ -69,33 +71,16 @@ constexpr int kSmemHalf = 115712;  // per block when two share an SM's 228 KB (1
 constexpr int kDefaultCtasPerSm = T2SC_CTAS_PER_SM;
 constexpr int kModeTf32x3 = kEpiF32;  // beside T2SC_DT_F16 (1) and T2SC_DT_BF16 (2)
 constexpr int kCopyWarp0 = 4;
-// Warp roles: 0-3 epilogue (warp q reads TMEM lane quadrant q); kCopyWarps
-// copy warps (8 in the 16-bit modes, 4 in the split-TF32 mode, whose
-// epilogue needs the registers); one control warp (weight copies, index
-// prefetch); one MMA warp.
-//
-// A warp issues from scheduler (SM sub-partition) warp % 4. The MMA warp
-// issues every tcgen05.mma of the CTA from one thread and the conv runs at
-// that thread's pace, so in the 16-bit modes (SPLIT layout) it sits on
-// sub-partition 1 with only the quadrant-1 epilogue warp (idle most of the
-// time), the control warp on 3 and the copy warps on 0, 2 and 3:
-//   warp  0 1 2 3 | 4 5   6 7 | 8 9    10 11 | 12 13   14 15
-//   role  E E E E | C MMA C C | C idle C  C  | C  idle C  control
-// 16 warps keep the pattern for a second CTA on the SM.
+// Warp roles: 0-3 epilogue; kCopyWarps copy warps (T2SC_COPY_WARPS in the
+// 16-bit modes, 4 in the split-TF32 mode); one control warp (weight copies,
+// index prefetch); one MMA warp.
 template <int DT, int RB = 128>
 struct Roles {
-  static constexpr bool kSplitLayout = DT != 3;
   // 16-byte vectors per row: each warp must own >= 32 / (RB / 16) rows
-  static constexpr int kCopyWarps = DT == 3 ? 4 : 8;
-  static constexpr int kControlWarp = kSplitLayout ? 15 : kCopyWarp0 + kCopyWarps;
-  static constexpr int kMmaWarp = kSplitLayout ? 5 : kControlWarp + 1;
-  static constexpr int kThreads = kSplitLayout ? 512 : 32 * (kMmaWarp + 1);
-  // copy-warp index of warp w, or -1
-  __device__ __forceinline__ static constexpr int copy_index(int w) {
-    return kSplitLayout ? (w == 4 ? 0 : w == 6 ? 1 : w == 7 ? 2 : w == 8 ? 3 : w == 10 ? 4 : w == 11 ? 5
-                                                                 : w == 12 ? 6 : w == 14 ? 7 : -1)
-                        : (w >= kCopyWarp0 && w < kCopyWarp0 + kCopyWarps ? w - kCopyWarp0 : -1);
-  }
+  static constexpr int kCopyWarps = DT == 3 ? 4 : T2SC_COPY_WARPS;
+  static constexpr int kControlWarp = kCopyWarp0 + kCopyWarps;
+  static constexpr int kMmaWarp = kControlWarp + 1;
+  static constexpr int kThreads = 32 * (kMmaWarp + 1);
 };
 
 struct TcArgs {
@@ -110,21 +95,12 @@ struct TcArgs {
   const uint32_t *tile_mask; // [ntiles]
   int64_t n_pad;
   int ntiles, ci, co, bn, nchunks, nco_tiles, kvol, stages, flags, tmem_cols;
-  // independent TMEM accumulators per tile (16-bit modes): consecutive MMA
-  // k-steps go to different ones, so no MMA waits on the previous one's
-  // result; the epilogue adds them
-  int nacc;
   uint32_t a_bytes, b_bytes, sub_bytes, stage_bytes;  // per (k, chunk) pair: A, B; pair slot; stage
   int group;                                          // (k, chunk) pairs per pipeline stage
 #if T2SC_CONV_DIAGNOSTICS
   int debug;  // diagnostics (T2SC_CONV_DEBUG): 1 skips the gathers, 2 the MMAs, 4 the epilogue stores
   long long *trace;  // diagnostics (T2SC_CONV_TRACE): per-stage clocks of CTA 0, or null
 #endif
-  int l1;          // gather through L1 (cp.async.ca) instead of L2 only (.cg)
-  int contiguous;  // CTA b takes units [b*U/G, (b+1)*U/G) instead of b, b+G, b+2G, ...
-  uint32_t backoff_epi, backoff_ctl, backoff_copy;  // sleep between polls of a waiting warp (ns; 0 = spin)
-  int wait_mode;   // how a waiting thread polls an mbarrier (sm100::mbar_wait_bounded)
-  int wait_elect;  // warps wait with one polling lane (1) or with every lane (0)
   int *err;
 };
 // Diagnostics build only (-DT2SC_CONV_DIAGNOSTICS=1, never the product
@@ -143,61 +119,18 @@ constexpr int kTraceN = 4096;
 #define T2SC_SKIP(bit) false
 #endif
 
-// Warp-uniform bounded wait. Every lane probes the barrier (the common
-// case, an already completed phase, costs one probe). Otherwise lane 0
-// alone polls, sleeping `backoff_ns` between polls so that a waiting warp
-// leaves the issue slots to the working ones, and the other lanes then
-// observe the completed phase themselves (each consumer lane acquires it).
-__device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, volatile int *abort, int *err,
-                                          uint32_t backoff_ns = 0, int g_wait_mode = 0, int elect = 0) {
-  if (elect) {
-    // lane 0 alone polls (one barrier operation per poll instead of 32);
-    // the warp barrier then orders the other lanes' later accesses after
-    // the phase lane 0 observed
-    bool ok = true;
-    if ((threadIdx.x & 31) == 0 && !sm100::mbar_test_wait(bar, parity))
-      ok = sm100::mbar_wait_bounded(bar, parity, abort, err, kDevErrTimeout, kWaitLimit, g_wait_mode);
-    ok = __shfl_sync(0xffffffffu, ok, 0);
-    __syncwarp();
-    return ok;
-  }
+// Warp-uniform bounded wait: every lane probes the barrier (the common
+// case, an already completed phase, costs one probe); a lane that has to
+// wait falls into the bounded loop; the verdict is agreed with a vote.
+__device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, volatile int *abort, int *err) {
   bool ok = sm100::mbar_test_wait(bar, parity);
   if (__all_sync(0xffffffffu, ok)) return true;
-  if (backoff_ns == 0) {
-    if (!ok) ok = sm100::mbar_wait_bounded(bar, parity, abort, err, kDevErrTimeout, kWaitLimit, g_wait_mode);
-    return __all_sync(0xffffffffu, ok);
-  }
-  int done = 0;
-  if ((threadIdx.x & 31) == 0) {
-    const long long t0 = clock64();
-    for (uint32_t i = 1;; i++) {
-      if (sm100::mbar_test_wait(bar, parity)) {
-        done = 1;
-        break;
-      }
-      __nanosleep(backoff_ns);
-      if ((i & 7) == 0) {
-        if (*abort) break;
-        if (clock64() - t0 > kWaitLimit) {
-          *abort = 1;
-          atomicOr(err, kDevErrTimeout);
-          break;
-        }
-      }
-    }
-  }
-  done = __shfl_sync(0xffffffffu, done, 0);
-  if (!done) return false;
-  ok = sm100::mbar_test_wait(bar, parity);
-  if (__all_sync(0xffffffffu, ok)) return true;
-  if (!ok) ok = sm100::mbar_wait_bounded(bar, parity, abort, err, kDevErrTimeout, kWaitLimit, g_wait_mode);
+  if (!ok) ok = sm100::mbar_wait_bounded(bar, parity, abort, err, kDevErrTimeout, kWaitLimit);
   return __all_sync(0xffffffffu, ok);
 }
 
-// NA: independent accumulators per tile (a.nacc, fixed at compile time so
-// the MMA thread spends no instructions choosing them).
-template <int DT, int RB, int NA>
-__global__ void __launch_bounds__(Roles<DT, RB>::kThreads, Roles<DT, RB>::kSplitLayout ? 2 : 1)
+template <int DT, int RB>
+__global__ void __launch_bounds__(Roles<DT, RB>::kThreads, 1)
     conv_tc_kernel(const TcArgs a) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // 1024-byte alignment for the swizzle atoms
@@ -248,19 +181,15 @@ __global__ void __launch_bounds__(Roles<DT, RB>::kThreads, Roles<DT, RB>::kSplit
   sm100::tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const int nunits = a.ntiles * a.nco_tiles;
-  const int ubeg = (int)((int64_t)blockIdx.x * nunits / gridDim.x);
-  const int uend = (int)((int64_t)(blockIdx.x + 1) * nunits / gridDim.x);
   // unit of this CTA's i-th iteration (nunits past its last one)
   auto unit_at = [&](int i) -> int {
-    if (a.contiguous) return ubeg + i < uend ? ubeg + i : nunits;
     const int64_t u = (int64_t)blockIdx.x + (int64_t)i * gridDim.x;
     return u < nunits ? (int)u : nunits;
   };
 
   // tile masks are read ahead so no global-load latency sits at a unit boundary
   auto mask_of = [&](int unit) -> uint32_t { return unit < nunits ? __ldg(a.tile_mask + unit / a.nco_tiles) : 0u; };
-  const int cw = Roles<DT, RB>::copy_index(warp);
-  if (cw >= 0) {
+  if (warp >= kCopyWarp0 && warp < kControlWarp) {
     // ----------------------------- copy warps -----------------------------
     // All copy warps fill every stage together: warp w owns tile rows
     // [w*RW, (w+1)*RW). Lane (rsub, j) copies 16-byte vector j of rows
@@ -272,6 +201,7 @@ __global__ void __launch_bounds__(Roles<DT, RB>::kThreads, Roles<DT, RB>::kSplit
     constexpr int RW = kTileRows / kW;    // rows per warp
     constexpr int RPL = RW * CPR / 32;    // rows per lane
     constexpr int EPV = 16 / ES;          // elements per vector
+    const int cw = warp - kCopyWarp0;
     const int j = lane % CPR, rsub = lane / CPR;
     const int row0 = cw * RW + rsub * RPL;
     uint32_t soff[RPL];
@@ -287,7 +217,7 @@ __global__ void __launch_bounds__(Roles<DT, RB>::kThreads, Roles<DT, RB>::kSplit
       uint32_t km = km_next;
       km_next = mask_of(unit_at(i + 1));
       const int npairs = __popc(km) * a.nchunks;
-      if (npairs > 0 && !warp_wait(idxf0 + 8 * (t & 1), (t >> 1) & 1, abort, a.err, 0, a.wait_mode, a.wait_elect)) {
+      if (npairs > 0 && !warp_wait(idxf0 + 8 * (t & 1), (t >> 1) & 1, abort, a.err)) {
         ok = false;
         break;
       }
@@ -296,12 +226,12 @@ __global__ void __launch_bounds__(Roles<DT, RB>::kThreads, Roles<DT, RB>::kSplit
       const uint8_t *gp[RPL];
       uint32_t gs[RPL];
       for (int q = 0; q < npairs && ok;) {
-        if (cw == 0 && lane == 0) T2SC_TRACE(0, cit);
-        if (!warp_wait(empty0 + 8 * s, ph ^ 1, abort, a.err, a.backoff_copy, a.wait_mode, a.wait_elect)) {
+        if (tid == 32 * kCopyWarp0) T2SC_TRACE(0, cit);
+        if (!warp_wait(empty0 + 8 * s, ph ^ 1, abort, a.err)) {
           ok = false;
           break;
         }
-        if (cw == 0 && lane == 0) T2SC_TRACE(1, cit);
+        if (tid == 32 * kCopyWarp0) T2SC_TRACE(1, cit);
         const uint32_t abase = sbase + s * a.stage_bytes, bar = full0 + 8 * s;
         const int valid = npairs - q < G ? npairs - q : G;
         for (int g = 0; g < valid; g++, q++) {
@@ -328,26 +258,23 @@ __global__ void __launch_bounds__(Roles<DT, RB>::kThreads, Roles<DT, RB>::kSplit
               gs[p] = src[p] >= 0 ? 16u : 0u;
             }
           }
-          if (cw == 0 && lane == 0) T2SC_TRACE(10, cit);
+          if (tid == 32 * kCopyWarp0) T2SC_TRACE(10, cit);
           const uint32_t sub = abase + g * a.sub_bytes;
           const bool cvalid = c * BKE + j * EPV < a.ci;
 #pragma unroll
           for (int p = 0; p < RPL; p++) {
             const uint32_t sz = cvalid ? gs[p] : 0u;
             if (T2SC_SKIP(1)) {
-            } else if (a.l1) {
-              sm100::cp_async_16_ca(sub + soff[p], gp[p] + c * RB, sz);
-              if (kSplit) sm100::cp_async_16_ca(sub + a_tile + soff[p], gp[p] + lo_delta + c * RB, sz);
             } else {
               sm100::cp_async_16(sub + soff[p], gp[p] + c * RB, sz);
               if (kSplit) sm100::cp_async_16(sub + a_tile + soff[p], gp[p] + lo_delta + c * RB, sz);
             }
           }
         }
-        if (cw == 0 && lane == 0) T2SC_TRACE(11, cit);
+        if (tid == 32 * kCopyWarp0) T2SC_TRACE(11, cit);
         // arrives on the stage barrier once this lane's copies have landed
         sm100::cp_async_arrive_noinc(bar);
-        if (cw == 0 && lane == 0) T2SC_TRACE(6, cit);
+        if (tid == 32 * kCopyWarp0) T2SC_TRACE(6, cit);
         cit++;
         if (++s == (uint32_t)S) {
           s = 0;
@@ -390,7 +317,7 @@ __global__ void __launch_bounds__(Roles<DT, RB>::kThreads, Roles<DT, RB>::kSplit
       if (u_next < nunits) {
         // the other buffer held unit t-1: wait until every copy warp is done with it
         const uint32_t nb = (t + 1) & 1;
-        if (!warp_wait(idxe0 + 8 * nb, (((t + 1) >> 1) & 1) ^ 1, abort, a.err, a.backoff_ctl, a.wait_mode, a.wait_elect)) {
+        if (!warp_wait(idxe0 + 8 * nb, (((t + 1) >> 1) & 1) ^ 1, abort, a.err)) {
           ok = false;
           break;
         }
@@ -406,7 +333,7 @@ __global__ void __launch_bounds__(Roles<DT, RB>::kThreads, Roles<DT, RB>::kSplit
       const uint8_t *wk = a.wimg;
       for (int q = 0; q < npairs && ok;) {
         if (lane == 0) T2SC_TRACE(7, it);
-        if (!warp_wait(empty0 + 8 * s, ph ^ 1, abort, a.err, a.backoff_ctl, a.wait_mode, a.wait_elect)) {
+        if (!warp_wait(empty0 + 8 * s, ph ^ 1, abort, a.err)) {
           ok = false;
           break;
         }
@@ -479,7 +406,7 @@ __global__ void __launch_bounds__(Roles<DT, RB>::kThreads, Roles<DT, RB>::kSplit
         bool ok = true;
         for (int kk = __popc(km); kk > 0; kk--) {
           const uint32_t b = acc_it & 1;
-          if (!warp_wait(tfull0 + 8 * b, (acc_it >> 1) & 1, abort, a.err, a.backoff_epi, a.wait_mode, a.wait_elect)) {
+          if (!warp_wait(tfull0 + 8 * b, (acc_it >> 1) & 1, abort, a.err)) {
             ok = false;
             break;
           }
@@ -516,11 +443,10 @@ __global__ void __launch_bounds__(Roles<DT, RB>::kThreads, Roles<DT, RB>::kSplit
       }
       const uint32_t b = acc_it & 1;
       if (tid == 0) T2SC_TRACE(4, acc_it);
-      if (!warp_wait(tfull0 + 8 * b, (acc_it >> 1) & 1, abort, a.err, a.backoff_epi, a.wait_mode, a.wait_elect)) break;
+      if (!warp_wait(tfull0 + 8 * b, (acc_it >> 1) & 1, abort, a.err)) break;
       if (tid == 0) T2SC_TRACE(5, acc_it);
       sm100::tc_fence_after();
-      const uint32_t tbase = tmem + ((uint32_t)(32 * q) << 16) + b * NA * a.bn;
-      constexpr int used = NA;  // every unit with work has >= RB / 32 >= NA k-steps
+      const uint32_t tbase = tmem + ((uint32_t)(32 * q) << 16) + b * a.bn;
       for (int cc = 0; cc < a.bn; cc += 16) {
         uint32_t r[16];
         sm100::tmem_ld16(tbase + cc, r);
@@ -528,12 +454,6 @@ __global__ void __launch_bounds__(Roles<DT, RB>::kThreads, Roles<DT, RB>::kSplit
         float acc[16];
 #pragma unroll
         for (int i = 0; i < 16; i++) acc[i] = __uint_as_float(r[i]);
-        for (int j = 1; j < used; j++) {
-          sm100::tmem_ld16(tbase + j * a.bn + cc, r);
-          sm100::tmem_ld_wait();
-#pragma unroll
-          for (int i = 0; i < 16; i++) acc[i] += __uint_as_float(r[i]);
-        }
         if (orow >= 0 && !T2SC_SKIP(4)) store16<DT>(a, orow, col0 + cc, acc);
       }
       sm100::tc_fence_before();
@@ -541,7 +461,7 @@ __global__ void __launch_bounds__(Roles<DT, RB>::kThreads, Roles<DT, RB>::kSplit
       if (lane == 0) sm100::mbar_arrive(tempty0 + 8 * b);
       acc_it++;
     }
-  } else if (warp == kMmaWarp) {
+  } else {
     // ----------------------------- MMA issuer -----------------------------
     if (lane == 0) {
       const uint32_t idesc =
@@ -563,24 +483,22 @@ __global__ void __launch_bounds__(Roles<DT, RB>::kThreads, Roles<DT, RB>::kSplit
         for (int gi = 0; gi < groups && ok; gi++) {
           const uint32_t b = acc_it & 1;
           if (!sm100::mbar_wait_bounded(tempty0 + 8 * b, ((acc_it >> 1) & 1) ^ 1, abort, a.err, kDevErrTimeout,
-                                        kWaitLimit, a.wait_mode)) {
+                                        kWaitLimit)) {
             ok = false;
             break;
           }
           sm100::tc_fence_after();
-          const uint32_t dtm = tmem + b * NA * a.bn;
-          uint32_t accum = 0;  // whether the accumulators hold data (the unit's first pair sets them)
-          uint32_t dacc[NA];   // the accumulators' TMEM addresses
-#pragma unroll
-          for (int j = 0; j < NA; j++) dacc[j] = dtm + j * a.bn;
+          const uint32_t dtm = tmem + b * a.bn;
+          uint32_t accum = 0;
           for (int q = 0; q < pairs_per_group; q += a.group) {
             T2SC_TRACE(2, mit);
-            if (!sm100::mbar_wait_bounded(full0 + 8 * s, ph, abort, a.err, kDevErrTimeout, kWaitLimit, a.wait_mode)) {
+            if (!sm100::mbar_wait_bounded(full0 + 8 * s, ph, abort, a.err, kDevErrTimeout, kWaitLimit)) {
               ok = false;
               break;
             }
             T2SC_TRACE(9, mit);
             sm100::tc_fence_after();
+            T2SC_TRACE(12, mit);
             const int valid = pairs_per_group - q < a.group ? pairs_per_group - q : a.group;
             for (int g = 0; g < valid; g++) {
               const uint64_t so = (s * a.stage_bytes + g * a.sub_bytes) >> 4;
@@ -594,14 +512,12 @@ __global__ void __launch_bounds__(Roles<DT, RB>::kThreads, Roles<DT, RB>::kSplit
                   sm100::mma_tf32(dtm, ahi, blo, idesc, 1u);
                   sm100::mma_tf32(dtm, ahi, bhi, idesc, 1u);
                 } else {
-                  // k-step kk of every pair goes to accumulator kk % nacc
-                  // (nacc divides RB / 32), cleared by the unit's first pair
-                  sm100::mma_f16(dacc[kk % NA], ahi, bhi, idesc, kk >= NA ? 1u : accum);
+                  sm100::mma_f16(dtm, ahi, bhi, idesc, accum);
                 }
-                if (kSplit) accum = 1;
+                accum = 1;
               }
-              accum = 1;
             }
+            T2SC_TRACE(13, mit);
             sm100::mma_commit(empty0 + 8 * s);
             T2SC_TRACE(3, mit);
             mit++;
@@ -647,9 +563,9 @@ __global__ void split_tf32_kernel(const float4 *__restrict__ x, float4 *__restri
   lo[i] = l;
 }
 
-template <int DT, int RB, int NA>
+template <int DT, int RB>
 int launch_tc(t2sc_conv *cv, const TcArgs &args, int grid, size_t smem, std::string &err) {
-  auto kfn = conv_tc_kernel<DT, RB, NA>;
+  auto kfn = conv_tc_kernel<DT, RB>;
   // set the shared-memory opt-in once per instantiation and size (a host-only
   // call kept out of the per-launch path, e.g. during stream capture)
   static int attr_smem[64] = {};
@@ -663,12 +579,12 @@ int launch_tc(t2sc_conv *cv, const TcArgs &args, int grid, size_t smem, std::str
   const char *trace_path = getenv("T2SC_CONV_TRACE");
   if (trace_path) {  // diagnostics only: allocates, synchronises and writes a file
     TcArgs t = args;
-    const size_t bytes = 12 * kTraceN * sizeof(long long);
+    const size_t bytes = 14 * kTraceN * sizeof(long long);
     T2SC_CUDA(cudaMalloc((void **)&t.trace, bytes), "trace");
     T2SC_CUDA(cudaMemset(t.trace, 0, bytes), "trace");
     kfn<<<grid, Roles<DT, RB>::kThreads, smem, cv->ctx->stream>>>(t);
     T2SC_LAUNCHED(cv->ctx, "conv_tc");
-    std::vector<long long> h(12 * kTraceN);
+    std::vector<long long> h(14 * kTraceN);
     T2SC_CUDA(cudaMemcpyAsync(h.data(), t.trace, bytes, cudaMemcpyDeviceToHost, cv->ctx->stream), "trace");
     T2SC_CUDA(cudaStreamSynchronize(cv->ctx->stream), "trace");
     cudaFree(t.trace);
@@ -784,35 +700,8 @@ int conv_tc_launch(t2sc_conv *cv, t2sc_map *m, const void *x, void *y, int flags
   a.debug = debug_bits;
   a.trace = nullptr;
 #endif
-  static const int l1_env = [] {
-    const char *e = getenv("T2SC_CONV_L1");
-    return e ? atoi(e) : 0;
-  }();
-  static const int contig_env = [] {
-    const char *e = getenv("T2SC_CONV_CONTIGUOUS");
-    return e ? atoi(e) : 0;
-  }();
-  static const int bo_env[3] = {
-      getenv("T2SC_BACKOFF_EPI") ? atoi(getenv("T2SC_BACKOFF_EPI")) : 0,
-      getenv("T2SC_BACKOFF_CTL") ? atoi(getenv("T2SC_BACKOFF_CTL")) : 0,
-      getenv("T2SC_BACKOFF_COPY") ? atoi(getenv("T2SC_BACKOFF_COPY")) : 0};
-  a.backoff_epi = bo_env[0];
-  a.backoff_ctl = bo_env[1];
-  a.backoff_copy = bo_env[2];
-  static const int wait_env = getenv("T2SC_WAIT_MODE") ? atoi(getenv("T2SC_WAIT_MODE")) : 0;
-  static const int elect_env = getenv("T2SC_WAIT_ELECT") ? atoi(getenv("T2SC_WAIT_ELECT")) : 0;
-  a.wait_elect = elect_env;
-  a.wait_mode = wait_env;
-  a.l1 = l1_env;
-
-  a.contiguous = contig_env;
-  // independent accumulators: up to the k-steps of a pair (RB / 32), within
-  // the SM's 512 TMEM columns (double-buffered, bn columns each)
-  static const int nacc_env = getenv("T2SC_CONV_NACC") ? atoi(getenv("T2SC_CONV_NACC")) : 4;
-  a.nacc = cv->dtype == T2SC_DT_F32 ? 1 : (nacc_env >= 4 ? 4 : nacc_env >= 2 ? 2 : 1);
-  while (a.nacc > 1 && (2 * a.nacc * cv->bn > 512 || a.nacc > cv->row_bytes / 32)) a.nacc >>= 1;
   int cols = 32;
-  while (cols < 2 * a.nacc * cv->bn) cols <<= 1;
+  while (cols < 2 * cv->bn) cols <<= 1;
   a.tmem_cols = cols;
   const int na = cv->dtype == T2SC_DT_F32 ? 2 : 1;
   a.a_bytes = kTileRows * cv->row_bytes * na;
@@ -835,16 +724,9 @@ int conv_tc_launch(t2sc_conv *cv, t2sc_map *m, const void *x, void *y, int flags
   int G = 1;
   if (cv->dtype != T2SC_DT_F32)
     while (G < 4 && (int)((G + 1) * a.sub_bytes) <= 48 * 1024 && avail / (int)((G + 1) * a.sub_bytes) >= 4) G++;
-  static const int group_env = getenv("T2SC_CONV_GROUP") ? atoi(getenv("T2SC_CONV_GROUP")) : 0;
-  if (group_env > 0 && cv->dtype != T2SC_DT_F32 && avail / (group_env * (int)a.sub_bytes) >= kMinStages) G = group_env;
   a.group = G;
   a.stage_bytes = G * a.sub_bytes;
   int S = avail / (int)a.stage_bytes;
-  static const int stages_env = [] {
-    const char *e = getenv("T2SC_CONV_STAGES");
-    return e ? atoi(e) : 8;
-  }();
-  if (S > stages_env) S = stages_env;
   if (S > 8) S = 8;
   if (S < kMinStages) {
     err = "conv tile does not fit shared memory";
@@ -880,30 +762,21 @@ int conv_tc_launch(t2sc_conv *cv, t2sc_map *m, const void *x, void *y, int flags
     T2SC_LAUNCHED(cv->ctx, "split_tf32");
     a.x = reinterpret_cast<const uint8_t *>(split);
     a.x_lo = reinterpret_cast<const uint8_t *>(split + cnt);
-    int rc = cv->row_bytes == 64 ? launch_tc<kModeTf32x3, 64, 1>(cv, a, grid, smem, err)
-                                 : launch_tc<kModeTf32x3, 32, 1>(cv, a, grid, smem, err);
+    int rc = cv->row_bytes == 64 ? launch_tc<kModeTf32x3, 64>(cv, a, grid, smem, err)
+                                 : launch_tc<kModeTf32x3, 32>(cv, a, grid, smem, err);
     return rc;
   }
   const bool bf = cv->dtype == T2SC_DT_BF16;
   switch (cv->row_bytes) {
     case 128:
-      if (a.nacc == 4)
-        return bf ? launch_tc<T2SC_DT_BF16, 128, 4>(cv, a, grid, smem, err)
-                  : launch_tc<T2SC_DT_F16, 128, 4>(cv, a, grid, smem, err);
-      if (a.nacc == 2)
-        return bf ? launch_tc<T2SC_DT_BF16, 128, 2>(cv, a, grid, smem, err)
-                  : launch_tc<T2SC_DT_F16, 128, 2>(cv, a, grid, smem, err);
-      return bf ? launch_tc<T2SC_DT_BF16, 128, 1>(cv, a, grid, smem, err)
-                : launch_tc<T2SC_DT_F16, 128, 1>(cv, a, grid, smem, err);
+      return bf ? launch_tc<T2SC_DT_BF16, 128>(cv, a, grid, smem, err)
+                : launch_tc<T2SC_DT_F16, 128>(cv, a, grid, smem, err);
     case 64:
-      if (a.nacc == 2)
-        return bf ? launch_tc<T2SC_DT_BF16, 64, 2>(cv, a, grid, smem, err)
-                  : launch_tc<T2SC_DT_F16, 64, 2>(cv, a, grid, smem, err);
-      return bf ? launch_tc<T2SC_DT_BF16, 64, 1>(cv, a, grid, smem, err)
-                : launch_tc<T2SC_DT_F16, 64, 1>(cv, a, grid, smem, err);
+      return bf ? launch_tc<T2SC_DT_BF16, 64>(cv, a, grid, smem, err)
+                : launch_tc<T2SC_DT_F16, 64>(cv, a, grid, smem, err);
     default:
-      return bf ? launch_tc<T2SC_DT_BF16, 32, 1>(cv, a, grid, smem, err)
-                : launch_tc<T2SC_DT_F16, 32, 1>(cv, a, grid, smem, err);
+      return bf ? launch_tc<T2SC_DT_BF16, 32>(cv, a, grid, smem, err)
+                : launch_tc<T2SC_DT_F16, 32>(cv, a, grid, smem, err);
   }
 }
 

@@ -156,103 +156,6 @@ __global__ void __launch_bounds__(kTileRows) sorted_nbr_kernel(int64_t n, int64_
   }
 }
 
-// Staged-window layout of one 128-row natural-order tile (one block of 256
-// threads). The tile's (row, offset) sources, read as 32-entry lines of
-// rows32, are sorted with their entry ids in shared memory (bitonic, 4096
-// 64-bit keys src << 12 | entry); distinct sources get consecutive window
-// slots in ascending row order, and a run starts wherever a source is not
-// its predecessor + 1. Writes each entry's slot, the run list and sizes,
-// the tile's offset mask, and flags a tile that exceeds the capacities.
-__global__ void __launch_bounds__(256) win_build_kernel(const int32_t *__restrict__ rows32,
-                                                       const uint32_t *__restrict__ mask, int64_t n, int kvol,
-                                                       int16_t *__restrict__ slot16, int32_t *__restrict__ runs,
-                                                       int32_t *__restrict__ meta, uint32_t *__restrict__ tmask,
-                                                       int *__restrict__ over) {
-  constexpr int NE = kTileRows * 32;  // entries of a tile (row, lane)
-  __shared__ unsigned long long key[NE];
-  __shared__ int2 part[256];
-  const int tid = threadIdx.x;
-  const int64_t base = (int64_t)blockIdx.x * kTileRows;
-  for (int e = tid; e < NE; e += 256) {
-    const int64_t r = base + (e >> 5);
-    const int32_t src = r < n ? rows32[r * 32 + (e & 31)] : -1;
-    key[e] = src >= 0 ? ((unsigned long long)src << 12) | (unsigned)e : ~0ull;
-  }
-  __syncthreads();
-  for (int k = 2; k <= NE; k <<= 1)
-    for (int j = k >> 1; j > 0; j >>= 1) {
-      for (int i = tid; i < NE; i += 256) {
-        const int ixj = i ^ j;
-        if (ixj > i) {
-          const unsigned long long a = key[i], b = key[ixj];
-          if ((a > b) == ((i & k) == 0)) key[i] = b, key[ixj] = a;
-        }
-      }
-      __syncthreads();
-    }
-  // flags per entry: first of its source (a new slot), first of a run
-  constexpr int PER = NE / 256;
-  int ns[PER], nr[PER];
-  int2 sum = make_int2(0, 0);
-  for (int q = 0; q < PER; q++) {
-    const int i = tid * PER + q;
-    const unsigned long long kv = key[i];
-    const bool valid = kv != ~0ull;
-    const long long src = (long long)(kv >> 12);
-    const long long prev = i > 0 && key[i - 1] != ~0ull ? (long long)(key[i - 1] >> 12) : -2;
-    ns[q] = valid && src != prev;
-    nr[q] = ns[q] && src != prev + 1;
-    sum.x += ns[q];
-    sum.y += nr[q];
-  }
-  part[tid] = sum;
-  __syncthreads();
-  if (tid < 32) {  // exclusive scan of the 256 partial sums by one warp
-    int2 v[8], run = make_int2(0, 0);
-    for (int q = 0; q < 8; q++) v[q] = part[tid * 8 + q], run.x += v[q].x, run.y += v[q].y;
-    int2 incl = run;
-    for (int d = 1; d < 32; d <<= 1) {
-      const int ax = __shfl_up_sync(0xffffffffu, incl.x, d), ay = __shfl_up_sync(0xffffffffu, incl.y, d);
-      if (tid >= d) incl.x += ax, incl.y += ay;
-    }
-    int2 acc = make_int2(incl.x - run.x, incl.y - run.y);
-    for (int q = 0; q < 8; q++) {
-      const int2 t = v[q];
-      part[tid * 8 + q] = acc;
-      acc.x += t.x, acc.y += t.y;
-    }
-    if (tid == 31) {
-      meta[blockIdx.x * 2] = incl.y;      // runs
-      meta[blockIdx.x * 2 + 1] = incl.x;  // window rows
-      if (incl.x > kWinRows || incl.y > kWinRunCap) atomicOr(over, 1);
-    }
-  }
-  __syncthreads();
-  int2 acc = part[tid];
-  for (int q = 0; q < PER; q++) {
-    const int i = tid * PER + q;
-    acc.x += ns[q];
-    acc.y += nr[q];
-    const unsigned long long kv = key[i];
-    if (kv == ~0ull) continue;
-    const int slot = acc.x - 1, e = (int)(kv & 4095u);
-    if (slot < kWinRows && (e & 31) < kvol)
-      slot16[((int64_t)blockIdx.x * kvol + (e & 31)) * kTileRows + (e >> 5)] = (int16_t)slot;
-    if (nr[q] && acc.y - 1 < kWinRunCap) {
-      int32_t *rp = runs + ((int64_t)blockIdx.x * kWinRunCap + acc.y - 1) * 2;
-      rp[0] = (int32_t)(kv >> 12);
-      rp[1] = slot;
-    }
-  }
-  if (tid < 32) {
-    uint32_t m = 0;
-    for (int p = tid; p < kTileRows; p += 32)
-      if (base + p < n) m |= mask[base + p];
-    m = __reduce_or_sync(0xffffffffu, m);
-    if (tid == 0) tmask[blockIdx.x] = m;
-  }
-}
-
 // pos[perm[p]] = p: sorted position of every target row (for the exports,
 // which list edges in the reference's row order).
 __global__ void inverse_perm_kernel(const int32_t *__restrict__ perm, int64_t n_pad, int32_t *__restrict__ pos) {
@@ -268,14 +171,6 @@ __global__ void iota_kernel(int32_t *v, int64_t n) {
   if (i < n) v[i] = (int32_t)i;
 }
 
-// Sort key of a row for the tile order: (row / chunk) in the high bits, the
-// occupancy mask in the low kbits, so rows are grouped by neighbour pattern
-// only inside runs of `chunk` consecutive (spatially close) rows.
-__global__ void chunk_key_kernel(const uint32_t *__restrict__ mask, int64_t n, int64_t chunk, int kbits,
-                                 uint64_t *__restrict__ key) {
-  int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (i < n) key[i] = ((uint64_t)(i / chunk) << kbits) | mask[i];
-}
 
 __global__ void edge_flags_kernel(const int32_t *__restrict__ nbr_sorted, const int32_t *__restrict__ pos, int64_t n,
                                   int64_t n_pad, int64_t total, int32_t *__restrict__ flags) {
@@ -361,11 +256,6 @@ void free_map(t2sc_map *m) {
   cudaFreeAsync(m->perm, st);
   cudaFreeAsync(m->nbr_sorted, st);
   cudaFreeAsync(m->tile_mask, st);
-  if (m->slot16) cudaFreeAsync(m->slot16, st);
-  if (m->win_runs) cudaFreeAsync(m->win_runs, st);
-  if (m->win_meta) cudaFreeAsync(m->win_meta, st);
-  if (m->tile_mask_nat) cudaFreeAsync(m->tile_mask_nat, st);
-  if (m->d_win_over) cudaFreeAsync(m->d_win_over, st);
   delete m;
 }
 
@@ -379,17 +269,6 @@ int map_edges(t2sc_map *m, int64_t *n_edges, std::string &err) {
     m->n_edges = (int64_t)e;
   }
   *n_edges = m->n_edges;
-  return T2SC_OK;
-}
-
-int map_win_ok(t2sc_map *m, int *ok, std::string &err) {
-  if (m->win_ok < 0) {
-    int over = 1;
-    T2SC_CUDA(cudaMemcpyAsync(&over, m->d_win_over, sizeof(int), cudaMemcpyDeviceToHost, m->ctx->stream), "win flag");
-    T2SC_CUDA(cudaStreamSynchronize(m->ctx->stream), "win flag");
-    m->win_ok = over ? 0 : 1;
-  }
-  *ok = m->win_ok;
   return T2SC_OK;
 }
 
@@ -472,58 +351,25 @@ int build_map(t2sc_coords *c, int kd, int kh, int kw, int dil, t2sc_map **out, s
     size_t temp_bytes = 0;
     T2SC_CUDA(cudaMallocAsync((void **)&iota, sizeof(int32_t) * n, st), "sort scratch");
     T2SC_CUDA(cudaMallocAsync((void **)&sorted, sizeof(int32_t) * n, st), "sort scratch");
-    iota_kernel<<<nblk(n, 256), 256, 0, st>>>(ctx->tile_order == kOrderNatural ? sorted : iota, n);
+    iota_kernel<<<nblk(n, 256), 256, 0, st>>>(iota, n);
     T2SC_LAUNCHED(ctx, "iota");
-    if (ctx->tile_order == kOrderMask) {
-      // stable LSD radix sort of rows by their occupancy mask (K key bits)
-      uint32_t *mask_sorted = nullptr;
-      T2SC_CUDA(cudaMallocAsync((void **)&mask_sorted, sizeof(uint32_t) * n, st), "sort scratch");
-      T2SC_CUDA(cub::DeviceRadixSort::SortPairs(nullptr, temp_bytes, m->mask, mask_sorted, iota, sorted, (int)n, 0,
-                                                K, st),
-                "sort size");
-      T2SC_CUDA(cudaMallocAsync(&temp, temp_bytes, st), "sort scratch");
-      T2SC_CUDA(cub::DeviceRadixSort::SortPairs(temp, temp_bytes, m->mask, mask_sorted, iota, sorted, (int)n, 0, K,
-                                                st),
-                "sort");
-      ctx->launches += 2 * ((K + 7) / 8) + 2;  // approximate CUB launch count (onesweep passes)
-      cudaFreeAsync(mask_sorted, st);
-    } else if (ctx->tile_order == kOrderChunked) {
-      const int64_t chunk = ctx->tile_chunk > 0 ? ctx->tile_chunk : 1024;
-      int cbits = 1;
-      while (((n + chunk - 1) / chunk) >> cbits) cbits++;
-      uint64_t *keys = nullptr, *keys_sorted = nullptr;
-      T2SC_CUDA(cudaMallocAsync((void **)&keys, sizeof(uint64_t) * n, st), "sort scratch");
-      T2SC_CUDA(cudaMallocAsync((void **)&keys_sorted, sizeof(uint64_t) * n, st), "sort scratch");
-      chunk_key_kernel<<<nblk(n, 256), 256, 0, st>>>(m->mask, n, chunk, K, keys);
-      T2SC_LAUNCHED(ctx, "chunk_key");
-      T2SC_CUDA(cub::DeviceRadixSort::SortPairs(nullptr, temp_bytes, keys, keys_sorted, iota, sorted, (int)n, 0,
-                                                K + cbits, st),
-                "sort size");
-      T2SC_CUDA(cudaMallocAsync(&temp, temp_bytes, st), "sort scratch");
-      T2SC_CUDA(cub::DeviceRadixSort::SortPairs(temp, temp_bytes, keys, keys_sorted, iota, sorted, (int)n, 0,
-                                                K + cbits, st),
-                "sort");
-      ctx->launches += 2 * ((K + cbits + 7) / 8) + 2;
-      cudaFreeAsync(keys, st);
-      cudaFreeAsync(keys_sorted, st);
-    }
+    // stable LSD radix sort of rows by their occupancy mask (K key bits):
+    // rows with the same neighbour pattern share tiles, so a tile visits few
+    // offsets (89 % of the issued MMA rows useful at the 512^3 shell, 42 %
+    // in coordinate order)
+    uint32_t *mask_sorted = nullptr;
+    T2SC_CUDA(cudaMallocAsync((void **)&mask_sorted, sizeof(uint32_t) * n, st), "sort scratch");
+    T2SC_CUDA(cub::DeviceRadixSort::SortPairs(nullptr, temp_bytes, m->mask, mask_sorted, iota, sorted, (int)n, 0, K,
+                                              st),
+              "sort size");
+    T2SC_CUDA(cudaMallocAsync(&temp, temp_bytes, st), "sort scratch");
+    T2SC_CUDA(cub::DeviceRadixSort::SortPairs(temp, temp_bytes, m->mask, mask_sorted, iota, sorted, (int)n, 0, K, st),
+              "sort");
+    ctx->launches += 2 * ((K + 7) / 8) + 2;  // approximate CUB launch count (onesweep passes)
+    cudaFreeAsync(mask_sorted, st);
     sorted_nbr_kernel<<<(unsigned)m->ntiles, kTileRows, 0, st>>>(n, m->n_pad, K, sorted, m->mask, rows32, m->perm,
                                                                  m->nbr_sorted, m->tile_mask);
     T2SC_LAUNCHED(ctx, "sorted_nbr");
-    if (ctx->conv_win) {  // staged-window layout for conv_win.cu
-      const size_t nt = (size_t)m->ntiles;
-      T2SC_CUDA(cudaMallocAsync((void **)&m->slot16, sizeof(int16_t) * K * (size_t)m->n_pad, st), "win map");
-      T2SC_CUDA(cudaMallocAsync((void **)&m->win_runs, sizeof(int32_t) * 2 * kWinRunCap * nt, st), "win map");
-      T2SC_CUDA(cudaMallocAsync((void **)&m->win_meta, sizeof(int32_t) * 2 * nt, st), "win map");
-      T2SC_CUDA(cudaMallocAsync((void **)&m->tile_mask_nat, sizeof(uint32_t) * nt, st), "win map");
-      T2SC_CUDA(cudaMallocAsync((void **)&m->d_win_over, sizeof(int), st), "win map");
-      T2SC_CUDA(cudaMemsetAsync(m->slot16, 0xff, sizeof(int16_t) * K * (size_t)m->n_pad, st), "win map");
-      T2SC_CUDA(cudaMemsetAsync(m->d_win_over, 0, sizeof(int), st), "win map");
-      win_build_kernel<<<(unsigned)nt, 256, 0, st>>>(rows32, m->mask, n, K, m->slot16, m->win_runs,
-                                                     m->win_meta, m->tile_mask_nat, m->d_win_over);
-      T2SC_LAUNCHED(ctx, "win_build");
-      m->win_ok = -1;
-    }
     cudaFreeAsync(rows32, st);
     if (temp) cudaFreeAsync(temp, st);
     cudaFreeAsync(sorted, st);

@@ -14,16 +14,6 @@ namespace t2sc {
 
 constexpr int kTileRows = 128;  // output rows per conv tile (UMMA M)
 constexpr int kMaxK = 32;       // kernel volume must fit a 32-bit offset mask
-constexpr int kWinRows = 512;   // staged-window capacity per tile (rows of 128 bytes)
-constexpr int kWinRunCap = 128; // contiguous source runs per tile
-
-// Order of output rows inside conv tiles (a performance choice: the set of
-// terms each output row sums, and their order, do not depend on it).
-enum TileOrder : int {
-  kOrderMask = 0,     // rows sorted by neighbour occupancy mask (fewest wasted MMA rows)
-  kOrderNatural = 1,  // rows in coordinate order (most source-row reuse inside a tile)
-  kOrderChunked = 2,  // mask-sorted inside runs of tile_chunk consecutive rows
-};
 
 // Device-side error flags (bit set by kernels, read by the host after a
 // launch sequence). Kernels never trap; they record and return.
@@ -50,9 +40,6 @@ struct t2sc_ctx {
   cudaStream_t stream = nullptr;
   int *d_err = nullptr;      // device error flags (one int)
   int64_t launches = 0;      // kernels launched by this context
-  int tile_order = 0;        // TileOrder of the conv maps built on this context
-  int conv_win = 0;          // build staged-window layouts with the maps and use conv_win.cu where it applies
-  int64_t tile_chunk = 1024; // rows per run for kOrderChunked
   std::string last_error;
   // identity row maps of the linear layers, one per row count, shared by
   // every linear handle of the context and kept until it is destroyed
@@ -76,18 +63,6 @@ struct t2sc_map {
   int32_t *perm = nullptr;       // [n_pad]   sorted position -> row (-1 padding)
   int32_t *nbr_sorted = nullptr; // [K][n_pad] source row of offset k for sorted position p (-1 = miss)
   uint32_t *tile_mask = nullptr; // [ntiles]  OR of masks in each 128-row tile
-  // Staged-window layout (conv_win.cu): tiles of 128 consecutive target rows
-  // in their own order; a tile's distinct source rows, in ascending order,
-  // are its window (runs of consecutive rows copied in bulk), and slot16
-  // gives each (offset, target) the window slot of its source (-1: none).
-  // Built with the map when win_ok; win_ok = 0 when some tile's window or
-  // run list exceeds the kernel's capacity (that map keeps the other kernel).
-  int win_ok = 0;                 // -1: capacity flag still on the device (d_win_over)
-  int *d_win_over = nullptr;
-  int16_t *slot16 = nullptr;      // [ntiles][K][128]: one contiguous block per tile
-  int32_t *win_runs = nullptr;    // [ntiles][kWinRunCap][2]: first source row, first slot
-  int32_t *win_meta = nullptr;    // [ntiles][2]: runs, window rows
-  uint32_t *tile_mask_nat = nullptr;  // [ntiles] OR of masks over the natural-order tile
 };
 
 struct t2sc_coords {
@@ -124,9 +99,7 @@ int build_map(t2sc_coords *c, int kd, int kh, int kw, int dil, t2sc_map **out, s
 void free_map(t2sc_map *m);
 // Edge count of a map (reads it back from the device once: synchronises).
 int map_edges(t2sc_map *m, int64_t *n_edges, std::string &err);
-// Whether the map's staged-window layout fits the window kernel (reads the
-// capacity flag back once: synchronises on the first call).
-int map_win_ok(t2sc_map *m, int *ok, std::string &err);
+
 // One-offset map with nbr[0][r] = r for rows [0, n): a linear layer run
 // through the conv kernels (dense rows, no coordinates).
 int build_identity_map(t2sc_ctx *ctx, int64_t n, t2sc_map **out, std::string &err);
@@ -150,10 +123,7 @@ int conv_tc_prepare(t2sc_conv *cv, const float *w_host, std::string &err);
 int conv_tc_launch(t2sc_conv *cv, t2sc_map *m, const void *x, void *y, int flags,
                    const void *residual, std::string &err);
 int conv_simt_prepare(t2sc_conv *cv, const float *w_host, std::string &err);
-// Staged-window tensor-core conv (conv_win.cu): 16-bit, Ci = Co = 64,
-// natural-order tiles; returns T2SC_ERR_UNSUPPORTED when it does not apply.
-int conv_win_launch(t2sc_conv *cv, t2sc_map *m, const void *x, void *y, int flags, const void *residual,
-                    std::string &err);
+
 int conv_simt_launch(t2sc_conv *cv, t2sc_map *m, const void *x, void *y, int flags,
                      const void *residual, std::string &err);
 

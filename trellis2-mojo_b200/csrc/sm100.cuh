@@ -67,17 +67,12 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t bar, uint32_t parit
 // Bounded wait: polls until the phase with `parity` completes, another
 // role raised `abort`, or ~`limit_cycles` SM clocks pass (then it raises
 // abort and ORs `err_bit` into *err). Returns false when it gave up.
-// mode 0 polls with the suspend-hinted try_wait, 1 with the plain try_wait,
-// 2 with the non-blocking test_wait.
 __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity, volatile int *abort, int *err,
-                                                  int err_bit, long long limit_cycles, int mode = 0) {
+                                                  int err_bit, long long limit_cycles) {
   if (mbar_test_wait(bar, parity)) return true;
   long long t0 = clock64();
   for (uint32_t i = 1;; i++) {
-    const bool done = mode == 0   ? mbar_try_wait_sleep(bar, parity)
-                      : mode == 1 ? mbar_try_wait(bar, parity)
-                                  : mbar_test_wait(bar, parity);
-    if (done) return true;
+    if (mbar_try_wait_sleep(bar, parity)) return true;
     if ((i & 3) == 0) {
       if (*abort) return false;
       if (clock64() - t0 > limit_cycles) {
@@ -102,10 +97,6 @@ __device__ __forceinline__ void cp_async_16(uint32_t dst, const void *src, uint3
   // no "memory" clobber: the copy's completion is ordered by the mbarrier
   // arrive that follows it, and the address math around it may interleave
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes));
-}
-// Same copy allocating in L1, so rows gathered again soon are served from it.
-__device__ __forceinline__ void cp_async_16_ca(uint32_t dst, const void *src, uint32_t src_bytes) {
-  asm volatile("cp.async.ca.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes));
 }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 template <int N>
@@ -170,31 +161,6 @@ __device__ __forceinline__ void mma_tf32(uint32_t d_tmem, uint64_t adesc, uint64
 __device__ __forceinline__ void mma_commit(uint32_t bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
 }
-
-// D[tmem] (+)= A[tmem] * B[smem desc]^T, kind::f16: the A operand read from
-// tensor memory (row m in lane m, two 16-bit elements of a row per column).
-__device__ __forceinline__ void mma_f16_ta(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
-                                           uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-
-// 32 lanes x 32 bit, 32 consecutive columns per thread (the warp's lane quadrant).
-__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
-      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
-      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
-      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]),
-      "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]),
-      "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
-      : "memory");
-}
-__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 // 32 lanes x 32 bit, 16 consecutive columns per thread.
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
