@@ -72,3 +72,25 @@ def test_noalloc_rejects_more_parents_than_its_scratch(t2sc):
                                                _ptr(dummy), ctypes.byref(m))
     assert rc == _lib.ERR_INVALID
     assert b"static scratch limit" in _lib.lib.t2sc_last_error(ctx.handle)
+
+
+def test_noalloc_at_the_static_parent_limit(t2sc):
+    """Exactly MAX_PARENTS parents (a 128 x 128 x 64 block of voxels): the
+    largest input the static scratch takes, bit-exact against the
+    allocating entry point."""
+    import torch
+    from t2sc import _lib
+    L = _lib.lib
+    ctx = t2sc.Context.default(0)
+    g = torch.stack(torch.meshgrid(torch.arange(128), torch.arange(128), torch.arange(64), indexing="ij"), -1)
+    g = g.reshape(-1, 3).to(torch.int32)
+    coords = torch.cat([torch.zeros((g.shape[0], 1), dtype=torch.int32), g], 1).contiguous().cuda()
+    assert coords.shape[0] == MAX_PARENTS
+    sub = torch.from_numpy(t2sc.synth.bernoulli(33, (MAX_PARENTS, 8))).cuda()
+    feats = torch.randn((MAX_PARENTS, 8), device="cuda").to(torch.bfloat16)
+    args = (ctx, coords, sub, feats, 8, _lib.FEATS_UPSAMPLE, _lib.DT_BF16, _lib.SUB_NONZERO)
+    ref = _run(t2sc, L.t2sc_subdivide_device, *args)
+    got = _run(t2sc, L.t2sc_subdivide_noalloc_device, *args)
+    assert got[0] == ref[0] > 3 * MAX_PARENTS
+    for a, b in zip(got[1:], ref[1:]):
+        assert torch.equal(a, b)

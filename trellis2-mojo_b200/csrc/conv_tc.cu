@@ -19,7 +19,7 @@
 //              stages are in flight. Thread 0 of the group also bulk-copies
 //              the pre-swizzled weight block (B tile) and prefetches each
 //              tile's neighbour-index block into shared memory a tile ahead;
-//   warp 8     TMEM owner and MMA issuer (one elected lane).
+//   warp 8     TMEM owner and MMA issuer (the converged warp; elect.sync issues).
 // Double-buffered TMEM accumulators let the epilogue of tile i overlap the
 // MMAs of tile i+1.
 //
@@ -463,7 +463,9 @@ __global__ void __launch_bounds__(Roles<DT, RB>::kThreads, 1)
     }
   } else {
     // ----------------------------- MMA issuer -----------------------------
-    if (lane == 0) {
+    // The whole warp runs this loop with warp-uniform values (waits agreed
+    // by vote); elect.sync picks the lane that issues each tcgen05 op.
+    {
       const uint32_t idesc =
           sm100::instr_desc(kSplit ? 2u : (DT == T2SC_DT_BF16 ? 1u : 0u), (uint32_t)a.bn);
       // descriptors of stage 0; a stage or k-step offset is added to the
@@ -482,8 +484,7 @@ __global__ void __launch_bounds__(Roles<DT, RB>::kThreads, 1)
         const int groups = kSplit ? nk : 1, pairs_per_group = kSplit ? a.nchunks : nk * a.nchunks;
         for (int gi = 0; gi < groups && ok; gi++) {
           const uint32_t b = acc_it & 1;
-          if (!sm100::mbar_wait_bounded(tempty0 + 8 * b, ((acc_it >> 1) & 1) ^ 1, abort, a.err, kDevErrTimeout,
-                                        kWaitLimit)) {
+          if (!warp_wait(tempty0 + 8 * b, ((acc_it >> 1) & 1) ^ 1, abort, a.err)) {
             ok = false;
             break;
           }
@@ -491,14 +492,14 @@ __global__ void __launch_bounds__(Roles<DT, RB>::kThreads, 1)
           const uint32_t dtm = tmem + b * a.bn;
           uint32_t accum = 0;
           for (int q = 0; q < pairs_per_group; q += a.group) {
-            T2SC_TRACE(2, mit);
-            if (!sm100::mbar_wait_bounded(full0 + 8 * s, ph, abort, a.err, kDevErrTimeout, kWaitLimit)) {
+            if (lane == 0) T2SC_TRACE(2, mit);
+            if (!warp_wait(full0 + 8 * s, ph, abort, a.err)) {
               ok = false;
               break;
             }
-            T2SC_TRACE(9, mit);
+            if (lane == 0) T2SC_TRACE(9, mit);
             sm100::tc_fence_after();
-            T2SC_TRACE(12, mit);
+            if (lane == 0) T2SC_TRACE(12, mit);
             const int valid = pairs_per_group - q < a.group ? pairs_per_group - q : a.group;
             for (int g = 0; g < valid; g++) {
               const uint64_t so = (s * a.stage_bytes + g * a.sub_bytes) >> 4;
@@ -508,18 +509,18 @@ __global__ void __launch_bounds__(Roles<DT, RB>::kThreads, 1)
                 if (T2SC_SKIP(2)) {
                 } else if (kSplit) {
                   const uint64_t alo = ahi + (a_tile >> 4), blo = bhi + (b_tile >> 4);
-                  sm100::mma_tf32(dtm, alo, bhi, idesc, accum);
-                  sm100::mma_tf32(dtm, ahi, blo, idesc, 1u);
-                  sm100::mma_tf32(dtm, ahi, bhi, idesc, 1u);
+                  sm100::mma_tf32_elect(dtm, alo, bhi, idesc, accum);
+                  sm100::mma_tf32_elect(dtm, ahi, blo, idesc, 1u);
+                  sm100::mma_tf32_elect(dtm, ahi, bhi, idesc, 1u);
                 } else {
-                  sm100::mma_f16(dtm, ahi, bhi, idesc, accum);
+                  sm100::mma_f16_elect(dtm, ahi, bhi, idesc, accum);
                 }
                 accum = 1;
               }
             }
-            T2SC_TRACE(13, mit);
-            sm100::mma_commit(empty0 + 8 * s);
-            T2SC_TRACE(3, mit);
+            if (lane == 0) T2SC_TRACE(13, mit);
+            sm100::mma_commit_elect(empty0 + 8 * s);
+            if (lane == 0) T2SC_TRACE(3, mit);
             mit++;
             if (++s == (uint32_t)S) {
               s = 0;
@@ -527,13 +528,13 @@ __global__ void __launch_bounds__(Roles<DT, RB>::kThreads, 1)
             }
           }
           if (!ok) break;
-          sm100::mma_commit(tfull0 + 8 * b);
+          sm100::mma_commit_elect(tfull0 + 8 * b);
           acc_it++;
         }
       }
       // all issued MMAs retire before TMEM is released
-      sm100::mma_commit(mma_done);
-      sm100::mbar_wait_cycles(mma_done, 0, kWaitLimit / 8);
+      sm100::mma_commit_elect(mma_done);
+      if (lane == 0) sm100::mbar_wait_cycles(mma_done, 0, kWaitLimit / 8);
     }
     __syncwarp();
   }
