@@ -252,9 +252,10 @@ def main():
     ap.add_argument("--impl", default="t2sc", choices=["t2sc", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extra", action="store_true", help="skip the cfg5 and cfg2 extra keys")
-    ap.add_argument("--op", default="conv", choices=["conv", "layernorm", "map", "subdiv"],
-                    help="layernorm / map / subdiv: time the LayerNorm+SiLU glue kernel, the coordinate hash + "
-                         "neighbour-map build (cfg4) or the subdivision (cfg5 parents) alone (not the headline)")
+    ap.add_argument("--op", default="conv", choices=["conv", "layernorm", "map", "subdiv", "glue"],
+                    help="layernorm / map / subdiv / glue: time the LayerNorm+SiLU glue kernel, the coordinate "
+                         "hash + neighbour-map build (cfg4), the subdivision (cfg5 parents) or the pipeline glue "
+                         "(trilinear sampler, cascade coordinates, FlexiDualGrid head) alone (not the headline)")
     args = ap.parse_args()
     if args.op == "layernorm":
         return run_layernorm(args)
@@ -262,6 +263,8 @@ def main():
         return run_map(args)
     if args.op == "subdiv":
         return run_subdiv(args)
+    if args.op == "glue":
+        return run_glue(args)
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
@@ -360,6 +363,89 @@ def run_subdiv(args):
                                  "includes": "one host synchronisation (child count)"},
                       "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": hbm, "peak_source": src,
                                    "unit": "GB/s", "frac": round(gbs / hbm, 4), "algorithmic_bytes": alg}}))
+
+
+def run_glue(args):
+    """The pipeline glue kernels, one JSON line each, with the oracle timed on
+    the same inputs on one host thread (kind "port"):
+      grid_sample: the cfg4 shell's 503,562 voxels (C = 6 f32 features, the
+        texture decoder's PBR channels) sampled at 2M points near the surface;
+        the coordinate hash is the handle's, built before timing.
+        Algorithmic bytes: L*12 query + L*C*4 out + N*C*4 features + hash.
+      cascade: 1,007,124 coordinates at resolution 512 (the cfg4 shell in two
+        batches) -> 64^3 tokens (lr 512, target 1024, budget 49152); includes
+        the two host read-backs. Algorithmic bytes: n*16 in + T*16 out.
+      fdg_head: 2M rows of 7 f32 channels. Algorithmic bytes: T*7*4 + T*7*4."""
+    import torch
+
+    import t2sc
+    from oracle import oracle as O
+    ctx = t2sc.Context.default(0)
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
+    ctx.set_stream(stream.cuda_stream)
+    S = t2sc.synth
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device="cuda")
+    _, hbm, src = peaks()
+    W = max(args.warmup, 3)
+
+    def line(name, ms, alg, workload, extra, cpu_s, cpu_sample):
+        gbs = alg / (ms * 1e-3) / 1e9
+        print(json.dumps({"metric": name, "value": round(ms, 4), "unit": "ms", "n_gpus": 1, "steps": args.steps,
+                          "warmup": W, "higher_is_better": False, "dtype": "f32 / int32", "data": "synthetic",
+                          "config": {"workload": workload, "l2": "flushed between steps (256 MiB write)", **extra},
+                          "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": hbm, "peak_source": src,
+                                       "unit": "GB/s", "frac": round(gbs / hbm, 4), "algorithmic_bytes": alg},
+                          "cpu_baseline": {"value": round(cpu_s * 1e3, 2), "unit": "ms", "cores": 1, "kind": "port",
+                                           "sample": cpu_sample}}), flush=True)
+
+    # ---- trilinear sampler ----
+    c = S.shell(*S.SHELLS["cfg4"])
+    n, C, L = len(c), 6, 2_000_000
+    xyz = np.ascontiguousarray(c[:, 1:])
+    feats = S.normal(42, (n, C))
+    rng = np.random.default_rng(1)
+    q = (xyz[rng.integers(0, n, L)] + rng.uniform(-1, 2, size=(L, 3))).astype(np.float32)
+    coords = t2sc.Coords(ctx, c)
+    df, dq = torch.from_numpy(feats).cuda(), torch.from_numpy(q).cuda()
+    ms = float(np.mean(timed(stream, lambda: t2sc.grid_sample_trilinear_device(coords, df, 512, dq), args.steps,
+                             W, flush)))
+    hcap = 1 << int(np.ceil(np.log2(max(2 * n, 1024))))
+    t0 = time.perf_counter()
+    O.grid_sample_trilinear(feats, xyz, 512, q[:200_000])
+    cpu = (time.perf_counter() - t0) * L / 200_000
+    line("trilinear sampler, cfg4 shell", ms, L * 12 + L * C * 4 + n * C * 4 + hcap * 16,
+         f"{n} voxels x {C} f32 channels sampled at {L} points", {"queries": L}, cpu,
+         "oracle on the first 200,000 queries, scaled to 2M")
+    # ---- cascade coordinates ----
+    c2 = c.copy()
+    c2[:, 0] = 1
+    c2[:, 1:] = (c2[:, 1:] + 37) % 512
+    hr = np.concatenate([c, c2])
+    dh = torch.from_numpy(hr).cuda()
+    res = {}
+
+    def cas():
+        res["out"] = t2sc.cascade_coords_device(dh, 512, 1024, 49152, ctx)
+
+    ms = float(np.mean(timed(stream, cas, args.steps, W, flush)))
+    T = len(res["out"][0])
+    t0 = time.perf_counter()
+    O.cascade_coords(hr, 512, 1024, 49152)
+    cpu = time.perf_counter() - t0
+    line("cascade coordinates, 512 -> 64^3 tokens", ms, len(hr) * 16 + T * 16,
+         f"{len(hr)} coordinates at 512 (2 batches) -> {T} tokens, target 1024, budget 49152",
+         {"includes": "two host read-backs (maximum q, token count)"}, cpu, "oracle on the whole input")
+    # ---- FlexiDualGrid head ----
+    Tn = 2_000_000
+    f7 = torch.from_numpy(S.normal(43, (Tn, 7), 4.0)).cuda()
+    ms = float(np.mean(timed(stream, lambda: t2sc.fdg_head_device(f7, 0.5, ctx), args.steps, W, flush)))
+    f7h = f7.cpu().numpy()
+    t0 = time.perf_counter()
+    O.fdg_head(f7h, 0.5)
+    cpu = time.perf_counter() - t0
+    line("FlexiDualGrid head", ms, Tn * 7 * 4 * 2, f"{Tn} rows x 7 f32 channels", {}, cpu,
+         "oracle on the whole input")
 
 
 def run_layernorm(args, rows=8_000_000, c=64):

@@ -293,6 +293,46 @@ int t2sc_halo_exchange_device(t2sc_comm *comm, void *feats, int64_t row_bytes, c
  * the communicator is aborted and T2SC_ERR_TIMEOUT / T2SC_ERR_CUDA returned. */
 int t2sc_comm_wait(t2sc_comm *comm, int timeout_ms);
 
+/* ---- pipeline glue around the decoder ----
+ * FlexiDualGrid head: replaces fdg_head (trellis2_mojo/models/sc_vaes/
+ * fdg_vae.mojo:17-50), the step of decode_shape (pipelines/image_to_3d.mojo:
+ * 206-216) after the decoder. feats device f32 [t, 7]; outputs device f32:
+ * vertices [t, 3] = (1 + 2*margin) * sigmoid(feats[:, 0:3]) - margin,
+ * intersected [t, 3] = 1.0 where feats[:, 3:6] > 0 else 0.0, quad_lerp
+ * [t, 1] = softplus(feats[:, 6]) (the value itself above 20). margin is
+ * rounded to f32 as in the reference. Asynchronous on the stream. */
+int t2sc_fdg_head_device(t2sc_ctx *ctx, const float *feats, int64_t t, double margin, float *vertices,
+                         float *intersected, float *quad_lerp);
+
+/* Cascade coordinates: replaces cascade_coords (trellis2_mojo/pipelines/
+ * image_to_3d.mojo:219-270), called by run_cascade_stage
+ * (run_image_to_3d.mojo:160-177) on the decoder's upsampled coordinates.
+ * hr_coords device int32 [n, 4] (b, x, y, z), all >= 0. For hr_resolution =
+ * resolution, resolution - 128, ...: q = int((xyz + 0.5) / lr_resolution *
+ * (hr_resolution / 16)) in f32, rows (b, q) deduplicated and sorted
+ * lexicographically; the first hr_resolution whose token count is below
+ * max_num_tokens, or 1024, is taken. out_coords device int32 [n, 4]
+ * receives *num_tokens rows; *hr_resolution (host) the resolution used.
+ * Synchronises the stream twice per tried resolution. Where the reference
+ * would loop without end (the budget never met and 1024 never reached)
+ * this returns T2SC_ERR_INVALID once hr_resolution / 16 reaches 0;
+ * max_num_tokens must be > 0; negative coordinates give T2SC_ERR_RANGE. */
+int t2sc_cascade_coords_device(t2sc_ctx *ctx, const int32_t *hr_coords, int64_t n, int lr_resolution,
+                               int resolution, int64_t max_num_tokens, int32_t *out_coords,
+                               int64_t *num_tokens, int *hr_resolution);
+
+/* Trilinear sampler: replaces grid_sample_trilinear (trellis2_mojo/meshing/
+ * vertex_attrs.mojo:46-104; flex_gemm grid_sample_3d, mode trilinear, B = 1)
+ * over the coordinate handle's own hash (rows of batch 0; a repeated voxel
+ * resolves to its last row, as the reference's dictionary does). feats
+ * device f32 [n, c] in the handle's row order; query device f32 [l, 3] in
+ * voxel units; out device f32 [l, c]. The 8 neighbours of p are p +- 0.5
+ * truncated toward zero; each weighs prod(1 - |n + 0.5 - p|); voxels absent,
+ * negative or >= grid_size weigh 0; the sum is divided by max(weight sum,
+ * 1e-12). grid_size <= 1536 (the hash's coordinate range). Asynchronous. */
+int t2sc_grid_sample_trilinear_device(t2sc_coords *coords, const float *feats, int c, int grid_size,
+                                      const float *query, int64_t l, float *out);
+
 /* ---- synthetic inputs (seeded shells of the benchmark configurations) ----
  * Active cells of a G^3 grid with | |p-c| - R(1 + 0.1 sin(3t) cos(2(f+phase))) | <= h,
  * c = G/2, t = acos((p_z-c)/|p-c|), f = atan2(p_y-c, p_x-c), phase = 0 for

@@ -65,6 +65,12 @@ def lib():
         L.orc_synth_normal.argtypes = [ctypes.c_uint64, ctypes.c_float, P, I64]
         L.orc_synth_bernoulli.restype = None
         L.orc_synth_bernoulli.argtypes = [ctypes.c_uint64, ctypes.c_double, P, I64]
+        L.orc_fdg_head.restype = None
+        L.orc_fdg_head.argtypes = [P, I64, ctypes.c_double, P, P, P]
+        L.orc_grid_sample_trilinear.restype = I
+        L.orc_grid_sample_trilinear.argtypes = [P, I64, I, P, I, P, I64, P]
+        L.orc_cascade_coords.restype = I64
+        L.orc_cascade_coords.argtypes = [P, I64, I, I, I64, P, ctypes.POINTER(ctypes.c_int)]
         _lib = L
     return _lib
 
@@ -263,3 +269,37 @@ def decoder(sd, model_channels, num_blocks, coords, x, guide_subs=None, pred_sub
             subs.append(pred if pred_subdiv else use)
     h = layernorm(h, None, None, eps=1e-5)
     return coords, linear(h, *g("output_layer")), subs
+
+
+def fdg_head(feats, voxel_margin=0.5):
+    """(vertices [T,3], intersected [T,3], quad_lerp [T,1]) of decoded [T,7]
+    features (models/sc_vaes/fdg_vae.mojo:17-50)."""
+    f = np.ascontiguousarray(feats, np.float32)
+    t = f.shape[0]
+    v, i, q = np.empty((t, 3), np.float32), np.empty((t, 3), np.float32), np.empty((t, 1), np.float32)
+    lib().orc_fdg_head(_p(f), t, voxel_margin, _p(v), _p(i), _p(q))
+    return v, i, q
+
+
+def grid_sample_trilinear(feats, coords_xyz, grid_size, query):
+    """[L, C] trilinear samples (meshing/vertex_attrs.mojo:46-104)."""
+    f = np.ascontiguousarray(feats, np.float32)
+    xyz = np.ascontiguousarray(coords_xyz, np.int32)
+    qy = np.ascontiguousarray(query, np.float32)
+    out = np.empty((qy.shape[0], f.shape[1]), np.float32)
+    rc = lib().orc_grid_sample_trilinear(_p(f), f.shape[0], f.shape[1], _p(xyz), grid_size, _p(qy), qy.shape[0],
+                                         _p(out))
+    assert rc == 0
+    return out
+
+
+def cascade_coords(hr_coords, lr_resolution, resolution, max_num_tokens):
+    """(coords [T,4] int32, hr_resolution) (pipelines/image_to_3d.mojo:219-270)."""
+    hr = np.ascontiguousarray(hr_coords, np.int32)
+    out = np.empty((max(hr.shape[0], 1), 4), np.int32)
+    res = ctypes.c_int()
+    t = lib().orc_cascade_coords(_p(hr), hr.shape[0], lr_resolution, resolution, max_num_tokens, _p(out),
+                                 ctypes.byref(res))
+    if t < 0:
+        raise ValueError("cascade_coords: token budget never met" if t == -2 else "allocation failed")
+    return out[:t].copy(), res.value

@@ -417,3 +417,110 @@ void orc_synth_bernoulli(uint64_t seed, double p, float *out, int64_t count) {
   orc_rng r = rng_seed(seed);
   for (int64_t i = 0; i < count; i++) out[i] = rng_f64(&r) < p ? 1.0f : 0.0f;
 }
+
+/* ---- pipeline glue around the decoder ---- */
+
+/* fdg_head, trellis2_mojo/models/sc_vaes/fdg_vae.mojo:17-50: f32 arithmetic
+ * with the reference's exp/log (libm expf/logf here). */
+void orc_fdg_head(const float *f, int64_t t, double margin, float *vert, float *inter, float *quad) {
+  const float m = (float)margin;
+  for (int64_t r = 0; r < t; r++) {
+    for (int c = 0; c < 3; c++) {
+      const float x = f[r * 7 + c];
+      vert[r * 3 + c] = (1.0f + 2.0f * m) / (1.0f + expf(-x)) - m;
+    }
+    for (int c = 0; c < 3; c++) inter[r * 3 + c] = f[r * 7 + 3 + c] > 0 ? 1.0f : 0.0f;
+    const float q = f[r * 7 + 6];
+    quad[r] = q > 20 ? q : logf(1.0f + expf(q));
+  }
+}
+
+/* The sampler's voxel lookup keys rows by (x << 42) | (y << 21) | z
+ * (vertex_attrs.mojo:40-43); rows are inserted in order with overwrite, so a
+ * repeated voxel keeps its last row (Dict). */
+/* grid_sample_trilinear, trellis2_mojo/meshing/vertex_attrs.mojo:46-104. */
+int orc_grid_sample_trilinear(const float *feats, int64_t n, int c, const int32_t *xyz, int grid, const float *query,
+                              int64_t l, float *out) {
+  static const float off[24] = {-0.5f, -0.5f, -0.5f, -0.5f, -0.5f, 0.5f, -0.5f, 0.5f, -0.5f, -0.5f, 0.5f, 0.5f,
+                                0.5f,  -0.5f, -0.5f, 0.5f,  -0.5f, 0.5f, 0.5f,  0.5f, -0.5f, 0.5f,  0.5f, 0.5f};
+  dict_t d;
+  dict_init(&d, n);
+  float *acc = (float *)malloc((size_t)c * sizeof(float));
+  if (!d.keys || !d.vals || !acc) { dict_free(&d); free(acc); return -1; }
+  for (int64_t i = 0; i < n; i++)
+    dict_put(&d, ((int64_t)xyz[3 * i] << 42) | ((int64_t)xyz[3 * i + 1] << 21) | (int64_t)xyz[3 * i + 2], i);
+  for (int64_t q = 0; q < l; q++) {
+    const float px = query[q * 3], py = query[q * 3 + 1], pz = query[q * 3 + 2];
+    for (int ch = 0; ch < c; ch++) acc[ch] = 0;
+    float wsum = 0;
+    for (int k = 0; k < 8; k++) {
+      const float fx = px + off[k * 3], fy = py + off[k * 3 + 1], fz = pz + off[k * 3 + 2];
+      if (!(fx > -1.0f && fy > -1.0f && fz > -1.0f)) continue;  /* truncates to a negative index: miss */
+      if (fx >= (float)grid || fy >= (float)grid || fz >= (float)grid) continue;
+      const int64_t nx = (int64_t)fx, ny = (int64_t)fy, nz = (int64_t)fz;  /* toward zero */
+      if (nx >= grid || ny >= grid || nz >= grid) continue;
+      const int64_t idx = dict_get(&d, (nx << 42) | (ny << 21) | nz);
+      if (idx < 0) continue;
+      const float w = (1.0f - fabsf((float)nx + 0.5f - px)) * (1.0f - fabsf((float)ny + 0.5f - py)) *
+                      (1.0f - fabsf((float)nz + 0.5f - pz));
+      wsum += w;
+      for (int ch = 0; ch < c; ch++) acc[ch] += w * feats[idx * c + ch];
+    }
+    const float denom = wsum < 1e-12f ? 1e-12f : wsum;
+    for (int ch = 0; ch < c; ch++) out[q * c + ch] = acc[ch] / denom;
+  }
+  dict_free(&d);
+  free(acc);
+  return 0;
+}
+
+static int cmp_i64(const void *a, const void *b) {
+  const int64_t x = *(const int64_t *)a, y = *(const int64_t *)b;
+  return x < y ? -1 : (x > y);
+}
+
+/* cascade_coords, trellis2_mojo/pipelines/image_to_3d.mojo:219-270. out
+ * [n, 4]; returns the token count (-1: allocation failure, -2: the budget
+ * is never met, where the reference would not terminate). */
+int64_t orc_cascade_coords(const int32_t *hr, int64_t n, int lr_res, int resolution, int64_t max_tokens,
+                           int32_t *out, int *hr_out) {
+  int64_t *qs = (int64_t *)malloc((size_t)(3 * n + 1) * sizeof(int64_t));
+  int64_t *keys = (int64_t *)malloc((size_t)(n + 1) * sizeof(int64_t));
+  if (!qs || !keys) { free(qs); free(keys); return -1; }
+  for (int hr_res = resolution;; hr_res -= 128) {
+    const int k = hr_res / 16;
+    if (k <= 0) { free(qs); free(keys); return -2; }
+    int64_t qmax = 0;
+    for (int64_t r = 0; r < n; r++)
+      for (int c = 1; c < 4; c++) {
+        const int64_t q = (int64_t)(((float)hr[r * 4 + c] + 0.5f) / (float)lr_res * (float)k);
+        qs[r * 3 + c - 1] = q;
+        if (q > qmax) qmax = q;
+      }
+    const int64_t m = qmax + 1;
+    for (int64_t r = 0; r < n; r++) {
+      int64_t key = hr[r * 4];
+      for (int c = 0; c < 3; c++) key = key * m + qs[r * 3 + c];
+      keys[r] = key;
+    }
+    qsort(keys, (size_t)n, sizeof(int64_t), cmp_i64);
+    int64_t tokens = 0;
+    for (int64_t i = 0; i < n; i++)
+      if (i == 0 || keys[i] != keys[i - 1]) tokens++;
+    if (tokens < max_tokens || hr_res == 1024) {
+      int64_t e = 0;
+      for (int64_t i = 0; i < n; i++) {
+        if (i > 0 && keys[i] == keys[i - 1]) continue;
+        int64_t key = keys[i];
+        out[e * 4 + 3] = (int32_t)(key % m); key /= m;
+        out[e * 4 + 2] = (int32_t)(key % m); key /= m;
+        out[e * 4 + 1] = (int32_t)(key % m);
+        out[e * 4 + 0] = (int32_t)(key / m);
+        e++;
+      }
+      *hr_out = hr_res;
+      free(qs); free(keys);
+      return tokens;
+    }
+  }
+}

@@ -94,6 +94,16 @@ int64_t orc_synth_shell(int g, double radius, double h, uint64_t seed, int batch
 void orc_synth_normal(uint64_t seed, float std_, float *out, int64_t count);
 void orc_synth_bernoulli(uint64_t seed, double p, float *out, int64_t count);
 
+/* Pipeline glue: fdg_head (models/sc_vaes/fdg_vae.mojo:17-50),
+ * grid_sample_trilinear (meshing/vertex_attrs.mojo:46-104, xyz int32 [n,3]),
+ * cascade_coords (pipelines/image_to_3d.mojo:219-270, hr int32 [n,4], out
+ * [n,4]; returns the token count, -2 where the reference never ends). */
+void orc_fdg_head(const float *f, int64_t t, double margin, float *vert, float *inter, float *quad);
+int orc_grid_sample_trilinear(const float *feats, int64_t n, int c, const int32_t *xyz, int grid, const float *query,
+                              int64_t l, float *out);
+int64_t orc_cascade_coords(const int32_t *hr, int64_t n, int lr_res, int resolution, int64_t max_tokens,
+                           int32_t *out, int *hr_out);
+
 #ifdef __cplusplus
 }
 #endif

@@ -193,3 +193,34 @@ def test_oracle_inputs_match_the_library_generator(oracle, t2sc):
             assert np.array_equal(a, b), (name, seed)
     assert np.array_equal(oracle.synth_normal(401, (27, 64), 0.1), t2sc.synth.normal(401, (27, 64), std=0.1))
     assert np.array_equal(oracle.synth_bernoulli(500, (1000, 8)), t2sc.synth.bernoulli(500, (1000, 8)))
+
+
+def test_pipeline_glue_hand_cases(oracle):
+    """The oracle's pipeline glue against cases worked by hand from
+    fdg_vae.mojo:17-50, vertex_attrs.mojo:46-104 and image_to_3d.mojo:219-270."""
+    f = np.zeros((3, 7), np.float32)
+    f[:, 6] = [20.5, 0.0, -3.0]
+    f[:, 3] = [1.0, 0.0, -1.0]
+    v, i, q = oracle.fdg_head(f, 0.5)
+    assert np.all(v == 0.5)  # (1 + 2m) * sigmoid(0) - m
+    assert i[:, 0].tolist() == [1.0, 0.0, 0.0]
+    np.testing.assert_allclose(q.ravel(), [20.5, np.log(2.0), np.log1p(np.exp(-3.0))], rtol=1e-6)
+
+    xyz = np.array([[1, 1, 1], [1, 2, 1], [2, 1, 1], [1, 1, 1]], np.int32)
+    feats = np.array([[0, 1], [2, 3], [4, 5], [6, 7]], np.float32)  # (1,1,1) resolves to its last row
+    q = np.array([[1.5, 1.5, 1.5], [1.5, 2.0, 1.5], [0.2, 0.2, 0.2], [9, 9, 9], [-0.9, 1.5, 1.5]], np.float32)
+    out = oracle.grid_sample_trilinear(feats, xyz, 4, q)
+    assert out[0].tolist() == [6.0, 7.0]
+    assert out[1].tolist() == [4.0, 5.0]  # half way between (1,1,1) and (1,2,1)
+    assert out[2].tolist() == [0.0, 0.0] and out[3].tolist() == [0.0, 0.0]
+    # x = -0.9: -1.4 truncates to -1 (a miss), -0.4 to 0 (absent): nothing found
+    assert out[4].tolist() == [0.0, 0.0]
+
+    hr = np.array([[0, 5, 5, 5], [0, 5, 5, 4], [0, 0, 0, 0], [1, 0, 0, 0], [0, 5, 5, 5]], np.int32)
+    c, res = oracle.cascade_coords(hr, 8, 1024, 100)  # k = 64: q = int((v + 0.5) * 8)
+    assert res == 1024
+    assert c.tolist() == [[0, 4, 4, 4], [0, 44, 44, 36], [0, 44, 44, 44], [1, 4, 4, 4]]
+    c, res = oracle.cascade_coords(hr, 8, 1536, 4)  # 4 tokens at every resolution: walks down to 1024
+    assert res == 1024
+    c, res = oracle.cascade_coords(hr, 8, 1536, 5)  # fits at once
+    assert res == 1536 and len(c) == 4

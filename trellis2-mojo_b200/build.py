@@ -9,7 +9,7 @@ import sys
 HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 OUT = os.path.join(HERE, "t2sc", "libt2sc.so")
-SOURCES = ["api.cu", "hashmap.cu", "scan.cu", "conv_tc.cu", "conv_simt.cu", "convert.cu", "subdiv.cu", "selftest.cu", "norm.cu", "dist.cu", "block.cu", "synth.cpp"]
+SOURCES = ["api.cu", "hashmap.cu", "scan.cu", "conv_tc.cu", "conv_simt.cu", "convert.cu", "subdiv.cu", "selftest.cu", "norm.cu", "dist.cu", "block.cu", "pipeline.cu", "synth.cpp"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

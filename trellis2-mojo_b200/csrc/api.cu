@@ -506,6 +506,50 @@ int t2sc_subdivide_device(t2sc_ctx *ctx, const int32_t *coords, int64_t n, const
   });
 }
 
+int t2sc_fdg_head_device(t2sc_ctx *ctx, const float *feats, int64_t t, double margin, float *vertices,
+                         float *intersected, float *quad_lerp) {
+  if (!ctx) return T2SC_ERR_INVALID;
+  if (t < 0) return fail(ctx, T2SC_ERR_INVALID, "fdg_head: t < 0");
+  if (t > 0 && (!feats || !vertices || !intersected || !quad_lerp))
+    return fail(ctx, T2SC_ERR_INVALID, "fdg_head: null buffer");
+  return guarded(ctx, [&]() -> int {
+    DeviceGuard g(ctx->device);
+    return fdg_head_device(ctx, feats, t, (float)margin, vertices, intersected, quad_lerp, ctx->last_error);
+  });
+}
+
+int t2sc_cascade_coords_device(t2sc_ctx *ctx, const int32_t *hr_coords, int64_t n, int lr_resolution,
+                               int resolution, int64_t max_num_tokens, int32_t *out_coords,
+                               int64_t *num_tokens, int *hr_resolution) {
+  if (!ctx) return T2SC_ERR_INVALID;
+  if (!num_tokens || !hr_resolution) return fail(ctx, T2SC_ERR_INVALID, "cascade_coords: null result pointer");
+  if (n < 0 || n >= (int64_t(1) << 31)) return fail(ctx, T2SC_ERR_INVALID, "cascade_coords: need 0 <= n < 2^31");
+  if (n > 0 && (!hr_coords || !out_coords)) return fail(ctx, T2SC_ERR_INVALID, "cascade_coords: null coordinates");
+  if (lr_resolution <= 0 || resolution <= 0 || resolution > (1 << 24))
+    return fail(ctx, T2SC_ERR_INVALID, "cascade_coords: need lr_resolution > 0 and 0 < resolution <= 2^24");
+  if (max_num_tokens <= 0) return fail(ctx, T2SC_ERR_INVALID, "cascade_coords: max_num_tokens must be > 0");
+  return guarded(ctx, [&]() -> int {
+    DeviceGuard g(ctx->device);
+    return cascade_coords_device(ctx, hr_coords, n, lr_resolution, resolution, max_num_tokens, out_coords,
+                                 num_tokens, hr_resolution, ctx->last_error);
+  });
+}
+
+int t2sc_grid_sample_trilinear_device(t2sc_coords *coords, const float *feats, int c, int grid_size,
+                                      const float *query, int64_t l, float *out) {
+  if (!coords) return T2SC_ERR_INVALID;
+  t2sc_ctx *ctx = coords->ctx;
+  if (c < 1 || l < 0) return fail(ctx, T2SC_ERR_INVALID, "grid_sample: need c >= 1 and l >= 0");
+  if (grid_size < 1 || grid_size > 1536)
+    return fail(ctx, T2SC_ERR_UNSUPPORTED, "grid_sample: grid_size must be in [1, 1536]");
+  if (l > 0 && (!query || !out || (coords->n > 0 && !feats)))
+    return fail(ctx, T2SC_ERR_INVALID, "grid_sample: null buffer");
+  return guarded(ctx, [&]() -> int {
+    DeviceGuard g(ctx->device);
+    return grid_sample_device(coords, feats, c, grid_size, query, l, out, ctx->last_error);
+  });
+}
+
 int t2sc_layernorm_device(t2sc_ctx *ctx, const void *x, void *y, int64_t rows, int c, const float *w,
                           const float *b, float eps, int flags, int dtype) {
   if (!ctx) return T2SC_ERR_INVALID;

@@ -219,6 +219,55 @@ __global__ void csr_emit_kernel(const int32_t *__restrict__ nbr_sorted, const in
 
 inline unsigned nblk(int64_t n, int t) { return (unsigned)((n + t - 1) / t); }
 
+// Trilinear sample of sparse voxel features at query points given in voxel
+// units (trellis2_mojo/meshing/vertex_attrs.mojo:46-104, the flex_gemm
+// grid_sample_3d semantics): the 8 neighbours are p +- 0.5 truncated toward
+// zero (for p < 0.5 two of them truncate to the same voxel and both count),
+// each weighs prod(1 - |n + 0.5 - p|); voxels absent from the set, negative
+// or >= grid_size weigh 0; the result is renormalised by the weight sum
+// clamped to 1e-12. Arithmetic in f32 in the reference's order (neighbours
+// k = 0..7 with x the slowest offset, the channel sums in k order), with the
+// roundings written out so that no multiply-add is contracted.
+__global__ void grid_sample_kernel(const longlong2 *__restrict__ slots, uint64_t hmask, const float *__restrict__ feats,
+                                   int c, int grid_size, const float *__restrict__ query, int64_t l,
+                                   float *__restrict__ out) {
+  const int64_t q = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (q >= l) return;
+  const float px = query[3 * q], py = query[3 * q + 1], pz = query[3 * q + 2];
+  int32_t idx[8];
+  float w[8];
+  float wsum = 0.f;
+#pragma unroll
+  for (int k = 0; k < 8; k++) {
+    idx[k] = -1;
+    w[k] = 0.f;
+    const float ox = (k & 4) ? 0.5f : -0.5f, oy = (k & 2) ? 0.5f : -0.5f, oz = (k & 1) ? 0.5f : -0.5f;
+    const float fx = __fadd_rn(px, ox), fy = __fadd_rn(py, oy), fz = __fadd_rn(pz, oz);
+    // a value outside int range cannot name a voxel: treat it as a miss
+    if (!(fx > -1.f && fy > -1.f && fz > -1.f && fx < (float)grid_size && fy < (float)grid_size &&
+          fz < (float)grid_size))
+      continue;
+    const int nx = (int)fx, ny = (int)fy, nz = (int)fz;  // truncation toward zero
+    if (nx >= grid_size || ny >= grid_size || nz >= grid_size) continue;
+    const int32_t r = hash_find(slots, hmask, pack_key(0, nx, ny, nz));
+    if (r < 0) continue;
+    const float wx = __fsub_rn(1.f, fabsf(__fsub_rn(__fadd_rn((float)nx, 0.5f), px)));
+    const float wy = __fsub_rn(1.f, fabsf(__fsub_rn(__fadd_rn((float)ny, 0.5f), py)));
+    const float wz = __fsub_rn(1.f, fabsf(__fsub_rn(__fadd_rn((float)nz, 0.5f), pz)));
+    idx[k] = r;
+    w[k] = __fmul_rn(__fmul_rn(wx, wy), wz);
+    wsum = __fadd_rn(wsum, w[k]);
+  }
+  const float denom = wsum < 1e-12f ? 1e-12f : wsum;
+  for (int ch = 0; ch < c; ch++) {
+    float acc = 0.f;
+#pragma unroll
+    for (int k = 0; k < 8; k++)
+      if (idx[k] >= 0) acc = __fadd_rn(acc, __fmul_rn(w[k], feats[(int64_t)idx[k] * c + ch]));
+    out[q * c + ch] = __fdiv_rn(acc, denom);
+  }
+}
+
 }  // namespace
 
 int build_hash(t2sc_coords *c, std::string &err) {
@@ -457,6 +506,16 @@ int export_csr(t2sc_coords *c, t2sc_map *m, int64_t *row_start, int64_t *src_s, 
   cudaFreeAsync(d_out, st);
   cudaFreeAsync(pos, st);
   T2SC_CUDA(cudaStreamSynchronize(st), "csr export");
+  return T2SC_OK;
+}
+
+int grid_sample_device(t2sc_coords *c, const float *feats, int ch, int grid_size, const float *query, int64_t l,
+                       float *out, std::string &err) {
+  t2sc_ctx *ctx = c->ctx;
+  if (l == 0) return T2SC_OK;
+  grid_sample_kernel<<<nblk(l, 256), 256, 0, ctx->stream>>>(c->d_slots, c->hcap - 1, feats, ch, grid_size, query, l,
+                                                          out);
+  T2SC_LAUNCHED(ctx, "grid_sample");
   return T2SC_OK;
 }
 

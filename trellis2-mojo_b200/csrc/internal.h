@@ -106,6 +106,10 @@ int build_identity_map(t2sc_ctx *ctx, int64_t n, t2sc_map **out, std::string &er
 int export_edges(t2sc_coords *c, t2sc_map *m, int64_t *src, int64_t *tgt, int64_t *kidx, std::string &err);
 int export_csr(t2sc_coords *c, t2sc_map *m, int64_t *row_start, int64_t *src_s, int64_t *kidx_s,
                std::string &err);
+// Trilinear sample of [n, ch] f32 features over the handle's hash (batch 0)
+// at l query points (f32 [l, 3], voxel units) into out [l, ch].
+int grid_sample_device(t2sc_coords *c, const float *feats, int ch, int grid_size, const float *query, int64_t l,
+                       float *out, std::string &err);
 
 // ---- exclusive scan of int32 counts into int64 offsets (scan.cu) ----
 // out[i] = sum(in[0..i)), *total (device int64) = sum(in). Scratch is
@@ -140,6 +144,13 @@ int subdivide_device(t2sc_ctx *ctx, const int32_t *coords, int64_t n, const floa
 // ---- LayerNorm (+ SiLU) (norm.cu) ----
 int layernorm_device(t2sc_ctx *ctx, const void *x, void *y, int64_t rows, int c, const float *w, const float *b,
                      float eps, int flags, int dtype, std::string &err);
+
+// ---- pipeline glue (pipeline.cu) ----
+int fdg_head_device(t2sc_ctx *ctx, const float *feats, int64_t t, float margin, float *vertices, float *intersected,
+                    float *quad, std::string &err);
+int cascade_coords_device(t2sc_ctx *ctx, const int32_t *hr_coords, int64_t n, int lr_resolution, int resolution,
+                          int64_t max_num_tokens, int32_t *out_coords, int64_t *num_tokens, int *hr_resolution,
+                          std::string &err);
 
 // ---- error-flag helpers (api.cu) ----
 int read_dev_err(t2sc_ctx *ctx, int *flags);

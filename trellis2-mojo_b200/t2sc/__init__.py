@@ -9,5 +9,7 @@ from .sparse import (Binarized, Context, LayerNorm32, Coords, SparseChannel2Spat
                      SparseUpsample, binarize, conv_chain, sparse_conv3d_from)
 from . import synth  # noqa: F401
 from .decoder import SparseConvNeXtBlock3d, SparseUnetVaeDecoder  # noqa: F401
+from .pipeline import (cascade_coords, cascade_coords_device, decode_shape, decode_tex, fdg_head,  # noqa: F401
+                       fdg_head_device, grid_sample_trilinear, grid_sample_trilinear_device)
 
 __version__ = "0.1"

@@ -53,6 +53,9 @@ SIGNATURES = {
     "t2sc_linear_create": (I32, [P, P, P, I32, I32, I32, PP]),
     "t2sc_linear_forward_device": (I32, [P, P, P, I64, I32, P]),
     "t2sc_layernorm_device": (I32, [P, P, P, I64, I32, P, P, F, I32, I32]),
+    "t2sc_fdg_head_device": (I32, [P, P, I64, D, P, P, P]),
+    "t2sc_cascade_coords_device": (I32, [P, P, I64, I32, I32, I64, P, PI64, ctypes.POINTER(ctypes.c_int)]),
+    "t2sc_grid_sample_trilinear_device": (I32, [P, P, I32, I32, P, I64, P]),
     "t2sc_convnext_block_create": (I32, [P, I32, I32, P, P, P, P, P, P, P, P, I32, PP]),
     "t2sc_convnext_block_destroy": (I32, [P]),
     "t2sc_convnext_block_forward_device": (I32, [P, P, P, P]),
