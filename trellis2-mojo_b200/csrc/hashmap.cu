@@ -228,43 +228,53 @@ inline unsigned nblk(int64_t n, int t) { return (unsigned)((n + t - 1) / t); }
 // clamped to 1e-12. Arithmetic in f32 in the reference's order (neighbours
 // k = 0..7 with x the slowest offset, the channel sums in k order), with the
 // roundings written out so that no multiply-add is contracted.
-__global__ void grid_sample_kernel(const longlong2 *__restrict__ slots, uint64_t hmask, const float *__restrict__ feats,
-                                   int c, int grid_size, const float *__restrict__ query, int64_t l,
-                                   float *__restrict__ out) {
-  const int64_t q = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (q >= l) return;
-  const float px = query[3 * q], py = query[3 * q + 1], pz = query[3 * q + 2];
-  int32_t idx[8];
-  float w[8];
-  float wsum = 0.f;
-#pragma unroll
-  for (int k = 0; k < 8; k++) {
-    idx[k] = -1;
-    w[k] = 0.f;
+// Eight lanes per query: lane k probes neighbour k, so the eight hash
+// probes of a query are in flight together; the weight sum and the channel
+// sums are then formed in neighbour order from shuffled (row, weight) pairs,
+// lane k producing channels k, k + 8, ... A missing neighbour adds an exact
+// 0 to the weight sum, which leaves it unchanged.
+__global__ void __launch_bounds__(256) grid_sample_kernel(const longlong2 *__restrict__ slots, uint64_t hmask,
+                                                          const float *__restrict__ feats, int c, int grid_size,
+                                                          const float *__restrict__ query, int64_t l,
+                                                          float *__restrict__ out) {
+  const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t q = t >> 3;
+  const int k = threadIdx.x & 7, lead = (threadIdx.x & 31) & ~7;
+  int32_t idx = -1;
+  float w = 0.f;
+  float px = 0.f, py = 0.f, pz = 0.f;
+  if (q < l) {
+    px = query[3 * q], py = query[3 * q + 1], pz = query[3 * q + 2];
     const float ox = (k & 4) ? 0.5f : -0.5f, oy = (k & 2) ? 0.5f : -0.5f, oz = (k & 1) ? 0.5f : -0.5f;
     const float fx = __fadd_rn(px, ox), fy = __fadd_rn(py, oy), fz = __fadd_rn(pz, oz);
-    // a value outside int range cannot name a voxel: treat it as a miss
-    if (!(fx > -1.f && fy > -1.f && fz > -1.f && fx < (float)grid_size && fy < (float)grid_size &&
-          fz < (float)grid_size))
-      continue;
-    const int nx = (int)fx, ny = (int)fy, nz = (int)fz;  // truncation toward zero
-    if (nx >= grid_size || ny >= grid_size || nz >= grid_size) continue;
-    const int32_t r = hash_find(slots, hmask, pack_key(0, nx, ny, nz));
-    if (r < 0) continue;
-    const float wx = __fsub_rn(1.f, fabsf(__fsub_rn(__fadd_rn((float)nx, 0.5f), px)));
-    const float wy = __fsub_rn(1.f, fabsf(__fsub_rn(__fadd_rn((float)ny, 0.5f), py)));
-    const float wz = __fsub_rn(1.f, fabsf(__fsub_rn(__fadd_rn((float)nz, 0.5f), pz)));
-    idx[k] = r;
-    w[k] = __fmul_rn(__fmul_rn(wx, wy), wz);
-    wsum = __fadd_rn(wsum, w[k]);
+    // a value that truncates below 0 or reaches grid_size names no voxel
+    if (fx > -1.f && fy > -1.f && fz > -1.f && fx < (float)grid_size && fy < (float)grid_size &&
+        fz < (float)grid_size) {
+      const int nx = (int)fx, ny = (int)fy, nz = (int)fz;  // truncation toward zero
+      const int32_t r = hash_find(slots, hmask, pack_key(0, nx, ny, nz));
+      if (r >= 0) {
+        const float wx = __fsub_rn(1.f, fabsf(__fsub_rn(__fadd_rn((float)nx, 0.5f), px)));
+        const float wy = __fsub_rn(1.f, fabsf(__fsub_rn(__fadd_rn((float)ny, 0.5f), py)));
+        const float wz = __fsub_rn(1.f, fabsf(__fsub_rn(__fadd_rn((float)nz, 0.5f), pz)));
+        idx = r;
+        w = __fmul_rn(__fmul_rn(wx, wy), wz);
+      }
+    }
   }
+  float wsum = 0.f;
+#pragma unroll
+  for (int j = 0; j < 8; j++) wsum = __fadd_rn(wsum, __shfl_sync(0xffffffffu, w, lead + j));
   const float denom = wsum < 1e-12f ? 1e-12f : wsum;
-  for (int ch = 0; ch < c; ch++) {
+  for (int c0 = 0; c0 < c; c0 += 8) {
+    const int ch = c0 + k;
     float acc = 0.f;
 #pragma unroll
-    for (int k = 0; k < 8; k++)
-      if (idx[k] >= 0) acc = __fadd_rn(acc, __fmul_rn(w[k], feats[(int64_t)idx[k] * c + ch]));
-    out[q * c + ch] = __fdiv_rn(acc, denom);
+    for (int j = 0; j < 8; j++) {
+      const int32_t rj = __shfl_sync(0xffffffffu, idx, lead + j);
+      const float wj = __shfl_sync(0xffffffffu, w, lead + j);
+      if (rj >= 0 && ch < c) acc = __fadd_rn(acc, __fmul_rn(wj, feats[(int64_t)rj * c + ch]));
+    }
+    if (q < l && ch < c) out[q * c + ch] = __fdiv_rn(acc, denom);
   }
 }
 
@@ -513,7 +523,7 @@ int grid_sample_device(t2sc_coords *c, const float *feats, int ch, int grid_size
                        float *out, std::string &err) {
   t2sc_ctx *ctx = c->ctx;
   if (l == 0) return T2SC_OK;
-  grid_sample_kernel<<<nblk(l, 256), 256, 0, ctx->stream>>>(c->d_slots, c->hcap - 1, feats, ch, grid_size, query, l,
+  grid_sample_kernel<<<nblk(l * 8, 256), 256, 0, ctx->stream>>>(c->d_slots, c->hcap - 1, feats, ch, grid_size, query, l,
                                                           out);
   T2SC_LAUNCHED(ctx, "grid_sample");
   return T2SC_OK;

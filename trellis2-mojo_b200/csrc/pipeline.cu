@@ -42,20 +42,29 @@ __global__ void fdg_head_kernel(const float *__restrict__ f, int64_t t, float m,
 __global__ void cascade_quant_kernel(const int4 *__restrict__ c, int64_t n, float lr, float k,
                                      int4 *__restrict__ q, int *__restrict__ maxima, int *err) {
   const int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (r >= n) return;
-  const int4 v = c[r];
-  if (v.x < 0 || v.y < 0 || v.z < 0 || v.w < 0) {
-    atomicOr(err, kDevErrRange);
-    return;
+  int mq = 0, mb = 0;  // every lane reaches the warp reduction below
+  if (r < n) {
+    const int4 v = c[r];
+    if (v.x < 0 || v.y < 0 || v.z < 0 || v.w < 0) {
+      atomicOr(err, kDevErrRange);
+    } else {
+      int4 o;
+      o.x = v.x;
+      o.y = (int)__fmul_rn(__fdiv_rn(__fadd_rn((float)v.y, 0.5f), lr), k);
+      o.z = (int)__fmul_rn(__fdiv_rn(__fadd_rn((float)v.z, 0.5f), lr), k);
+      o.w = (int)__fmul_rn(__fdiv_rn(__fadd_rn((float)v.w, 0.5f), lr), k);
+      q[r] = o;
+      mq = max(o.y, max(o.z, o.w));
+      mb = o.x;
+    }
   }
-  int4 o;
-  o.x = v.x;
-  o.y = (int)__fmul_rn(__fdiv_rn(__fadd_rn((float)v.y, 0.5f), lr), k);
-  o.z = (int)__fmul_rn(__fdiv_rn(__fadd_rn((float)v.z, 0.5f), lr), k);
-  o.w = (int)__fmul_rn(__fdiv_rn(__fadd_rn((float)v.w, 0.5f), lr), k);
-  q[r] = o;
-  atomicMax(&maxima[0], max(o.y, max(o.z, o.w)));
-  atomicMax(&maxima[1], o.x);
+  // one atomic per warp: a million same-address atomics serialise
+  mq = __reduce_max_sync(0xffffffffu, mq);
+  mb = __reduce_max_sync(0xffffffffu, mb);
+  if ((threadIdx.x & 31) == 0) {
+    atomicMax(&maxima[0], mq);
+    atomicMax(&maxima[1], mb);
+  }
 }
 
 __global__ void cascade_key_kernel(const int4 *__restrict__ q, int64_t n, uint64_t m, uint64_t *__restrict__ keys) {
