@@ -20,14 +20,20 @@ from _cases import F16_TOL, F32_TOL, conv_inputs, oracle_chain, rel_err
 pytestmark = pytest.mark.gpu
 
 
-@pytest.mark.parametrize("dtype", ["f32", "f16"])
+@pytest.mark.parametrize("dtype", ["f32", "f16", "f32_f16w"])
 def test_cfg2_residual_block(t2sc, oracle, dtype):
+    """f32_f16w: f32 activations with f16-exact weights (an f16 checkpoint,
+    gpu/conv.mojo:32-36), which the split-TF32 mode runs with two MMAs per
+    k-step instead of three."""
     S = t2sc.synth
     coords = S.shell(*S.SHELLS["cfg2"])
     n, c = len(coords), 256
     assert n == 101422
     x, w1, b1 = conv_inputs(S, n, c, c, seed=200)
     _, w2, b2 = conv_inputs(S, 1, c, c, seed=210)
+    if dtype == "f32_f16w":
+        w1, w2 = (w.astype(np.float16).astype(np.float32) for w in (w1, w2))
+        dtype = "f32"
     csr = oracle.csr(n, *oracle.neighbor_map(coords))
     convs = [t2sc.SparseConv3d(w1, b1, dtype=dtype), t2sc.SparseConv3d(w2, b2, dtype=dtype)]
     y = t2sc.conv_chain(convs, t2sc.SparseTensor(x, coords), [1, 2]).feats
