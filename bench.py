@@ -280,7 +280,9 @@ def run_map(args):
     change: t2sc_coords_create_device (hash insert + range check) and
     t2sc_coords_build_map (row masks, mask sort, sorted neighbour rows, edge
     count). Algorithmic bytes (the survey's B_map): N*16 coords in +
-    N*27*4 map out + 2*cap*12 hash (key + row, written then read)."""
+    N*27*4 map out + 2*cap*12 hash (key + row, written then read; cap = the
+    power of two >= 2N, a half-full table, independent of the library's own
+    sparser table)."""
     import torch
 
     import t2sc
@@ -410,7 +412,7 @@ def run_glue(args):
     df, dq = torch.from_numpy(feats).cuda(), torch.from_numpy(q).cuda()
     ms = float(np.mean(timed(stream, lambda: t2sc.grid_sample_trilinear_device(coords, df, 512, dq), args.steps,
                              W, flush)))
-    hcap = 1 << int(np.ceil(np.log2(max(2 * n, 1024))))
+    hcap = 1 << int(np.ceil(np.log2(max(2 * n, 1024))))  # a half-full table, whatever the library's
     t0 = time.perf_counter()
     O.grid_sample_trilinear(feats, xyz, 512, q[:200_000])
     cpu = (time.perf_counter() - t0) * L / 200_000

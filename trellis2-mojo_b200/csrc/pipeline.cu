@@ -39,7 +39,7 @@ __global__ void fdg_head_kernel(const float *__restrict__ f, int64_t t, float m,
 
 // q per row and axis, plus the largest q and batch index (for the key radix)
 // and a flag for negative inputs, which the key packing does not take.
-__global__ void cascade_quant_kernel(const int4 *__restrict__ c, int64_t n, float lr, float k,
+__global__ void __launch_bounds__(256) cascade_quant_kernel(const int4 *__restrict__ c, int64_t n, float lr, float k,
                                      int4 *__restrict__ q, int *__restrict__ maxima, int *err) {
   const int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   int mq = 0, mb = 0;  // every lane reaches the warp reduction below
@@ -58,12 +58,20 @@ __global__ void cascade_quant_kernel(const int4 *__restrict__ c, int64_t n, floa
       mb = o.x;
     }
   }
-  // one atomic per warp: a million same-address atomics serialise
+  // one atomic pair per block: same-address atomics serialise in L2
+  __shared__ int wq[8], wb[8];
   mq = __reduce_max_sync(0xffffffffu, mq);
   mb = __reduce_max_sync(0xffffffffu, mb);
-  if ((threadIdx.x & 31) == 0) {
-    atomicMax(&maxima[0], mq);
-    atomicMax(&maxima[1], mb);
+  if ((threadIdx.x & 31) == 0) wq[threadIdx.x >> 5] = mq, wb[threadIdx.x >> 5] = mb;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    const int nw = blockDim.x >> 5;
+    mq = __reduce_max_sync(0xffffffffu, threadIdx.x < nw ? wq[threadIdx.x] : 0);
+    mb = __reduce_max_sync(0xffffffffu, threadIdx.x < nw ? wb[threadIdx.x] : 0);
+    if (threadIdx.x == 0) {
+      atomicMax(&maxima[0], mq);
+      atomicMax(&maxima[1], mb);
+    }
   }
 }
 
