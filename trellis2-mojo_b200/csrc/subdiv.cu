@@ -8,8 +8,9 @@
 //
 // Three passes: (1) per parent, the 8-bit keep mask and its popcount;
 // (2) an exclusive shuffle-scan of the counts (scan.cu) gives each parent's
-// first output row; (3) children and their feature rows are written, the
-// features as 16-byte vectors when the row size allows.
+// first output row; (3) eight lanes per parent write its children and their
+// feature rows (16-byte vectors when the row size allows). The child count
+// is read back once, at the end.
 #include <mutex>
 
 #include "internal.h"
@@ -31,39 +32,63 @@ __global__ void sub_count_kernel(const float *__restrict__ sub, int64_t n, int p
   counts[r] = __popc(m);
 }
 
-__global__ void sub_emit_kernel(const int4 *__restrict__ coords, const uint8_t *__restrict__ masks,
-                                const int64_t *__restrict__ offs, int64_t n, int4 *__restrict__ out_coords,
-                                int32_t *__restrict__ parent, int32_t *__restrict__ subidx) {
-  int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (r >= n) return;
-  uint32_t m = masks[r];
-  if (!m) return;
-  int4 p = coords[r];
-  int64_t e = offs[r];
-  while (m) {
-    int c = __ffs(m) - 1;
-    m &= m - 1;
-    out_coords[e] = make_int4(p.x, p.y * 2 + (c & 1), p.z * 2 + ((c >> 1) & 1), p.w * 2 + ((c >> 2) & 1));
-    parent[e] = (int32_t)r;
-    subidx[e] = c;
-    e++;
-  }
-}
-
-// out[e, :] = in[parent[e], slot*C : slot*C + C] with slot = subidx[e] (C2S) or 0.
+// Eight lanes per parent (four parents per warp): lane c handles child slot
+// c; a kept child lands at row offs[r] + popcount(mask & ((1 << c) - 1)), so
+// children stay parent-major with c ascending. Each kept lane writes its
+// coordinates, parent / slot entries and its feature row (vpr vectors).
+// parent / subidx / in may be null (nothing written or copied for them).
 template <typename V>
-__global__ void sub_feats_kernel(const V *__restrict__ in, V *__restrict__ out, const int32_t *__restrict__ parent,
-                                 const int32_t *__restrict__ subidx, int64_t m, int vec_per_row, int c2s) {
-  int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= m * vec_per_row) return;
-  int64_t e = i / vec_per_row;
-  int v = (int)(i % vec_per_row);
-  int64_t p = parent[e];
-  int64_t src = c2s ? (p * 8 + subidx[e]) * vec_per_row + v : p * vec_per_row + v;
-  out[i] = in[src];
+__global__ void __launch_bounds__(256) sub_children_kernel(const int4 *__restrict__ coords,
+                                                           const uint8_t *__restrict__ masks,
+                                                           const int64_t *__restrict__ offs, int64_t n,
+                                                           const V *__restrict__ in, V *__restrict__ out, int vpr,
+                                                           int c2s, int4 *__restrict__ out_coords,
+                                                           int32_t *__restrict__ parent, int32_t *__restrict__ subidx) {
+  const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t r = t >> 3;
+  const int c = (int)(t & 7);
+  if (r >= n) return;
+  const uint32_t m = masks[r];
+  if (!((m >> c) & 1u)) return;
+  const int64_t e = offs[r] + __popc(m & ((1u << c) - 1u));
+  const int4 p = coords[r];
+  out_coords[e] = make_int4(p.x, p.y * 2 + (c & 1), p.z * 2 + ((c >> 1) & 1), p.w * 2 + ((c >> 2) & 1));
+  if (parent) parent[e] = (int32_t)r;
+  if (subidx) subidx[e] = c;
+  if (!in) return;
+  const V *src = in + (c2s ? (r * 8 + c) : r) * vpr;
+  V *dst = out + e * vpr;
+  for (int v = 0; v < vpr; v++) dst[v] = src[v];
 }
 
 inline unsigned nblk(int64_t n) { return (unsigned)((n + 255) / 256); }
+
+// Children, parent / slot entries and feature rows of every kept child, in
+// one launch (no host read of the child count needed first).
+int emit_children(t2sc_ctx *ctx, const int32_t *coords, const uint8_t *masks, const int64_t *offs, int64_t n,
+                  const void *feats, int c, int feats_mode, int dtype, int32_t *out_coords, void *out_feats,
+                  int32_t *par, int32_t *sidx, std::string &err) {
+  cudaStream_t st = ctx->stream;
+  const bool copy = feats_mode != T2SC_FEATS_NONE;
+  const int64_t row_bytes = copy ? (int64_t)c * (dtype == T2SC_DT_F32 ? 4 : 2) : 16;
+  const int c2s = feats_mode == T2SC_FEATS_C2S;
+  const unsigned grid = (unsigned)((n * 8 + 255) / 256);
+  if (row_bytes % 16 == 0) {
+    sub_children_kernel<uint4><<<grid, 256, 0, st>>>((const int4 *)coords, masks, offs, n,
+                                                     copy ? (const uint4 *)feats : nullptr, (uint4 *)out_feats,
+                                                     (int)(row_bytes / 16), c2s, (int4 *)out_coords, par, sidx);
+  } else if (row_bytes % 4 == 0) {
+    sub_children_kernel<uint32_t><<<grid, 256, 0, st>>>((const int4 *)coords, masks, offs, n,
+                                                        (const uint32_t *)feats, (uint32_t *)out_feats,
+                                                        (int)(row_bytes / 4), c2s, (int4 *)out_coords, par, sidx);
+  } else {
+    sub_children_kernel<uint16_t><<<grid, 256, 0, st>>>((const int4 *)coords, masks, offs, n,
+                                                        (const uint16_t *)feats, (uint16_t *)out_feats,
+                                                        (int)(row_bytes / 2), c2s, (int4 *)out_coords, par, sidx);
+  }
+  T2SC_LAUNCHED(ctx, "sub_children");
+  return T2SC_OK;
+}
 }  // namespace
 
 int subdivide_device(t2sc_ctx *ctx, const int32_t *coords, int64_t n, const float *sub, int keep_mode,
@@ -78,40 +103,18 @@ int subdivide_device(t2sc_ctx *ctx, const int32_t *coords, int64_t n, const floa
   T2SC_CUDA(cudaMallocAsync((void **)&masks, n, st), "subdiv scratch");
   T2SC_CUDA(cudaMallocAsync((void **)&counts, n * sizeof(int32_t), st), "subdiv scratch");
   T2SC_CUDA(cudaMallocAsync((void **)&offs, (n + 1) * sizeof(int64_t), st), "subdiv scratch");
-  if (!par) T2SC_CUDA(cudaMallocAsync((void **)&par, 8 * n * sizeof(int32_t), st), "subdiv scratch");
-  if (!sidx) T2SC_CUDA(cudaMallocAsync((void **)&sidx, 8 * n * sizeof(int32_t), st), "subdiv scratch");
   sub_count_kernel<<<nblk(n), 256, 0, st>>>(sub, n, keep_mode == T2SC_SUB_POSITIVE, masks, counts);
   T2SC_LAUNCHED(ctx, "sub_count");
   int rc = scan_counts(ctx, counts, n, offs, offs + n);
   if (rc != T2SC_OK) return rc;
-  sub_emit_kernel<<<nblk(n), 256, 0, st>>>((const int4 *)coords, masks, offs, n, (int4 *)out_coords, par, sidx);
-  T2SC_LAUNCHED(ctx, "sub_emit");
+  rc = emit_children(ctx, coords, masks, offs, n, feats, c, feats_mode, dtype, out_coords, out_feats, par, sidx, err);
+  if (rc != T2SC_OK) return rc;
   int64_t m = 0;
   T2SC_CUDA(cudaMemcpyAsync(&m, offs + n, sizeof(int64_t), cudaMemcpyDeviceToHost, st), "subdiv count");
   T2SC_CUDA(cudaStreamSynchronize(st), "subdiv count");
-  if (feats_mode != T2SC_FEATS_NONE && m > 0) {
-    const int64_t row_bytes = (int64_t)c * (dtype == T2SC_DT_F32 ? 4 : 2);
-    const int c2s = feats_mode == T2SC_FEATS_C2S;
-    if (row_bytes % 16 == 0) {
-      int vpr = (int)(row_bytes / 16);
-      sub_feats_kernel<uint4><<<nblk(m * vpr), 256, 0, st>>>((const uint4 *)feats, (uint4 *)out_feats, par, sidx, m,
-                                                            vpr, c2s);
-    } else if (row_bytes % 4 == 0) {
-      int vpr = (int)(row_bytes / 4);
-      sub_feats_kernel<uint32_t><<<nblk(m * vpr), 256, 0, st>>>((const uint32_t *)feats, (uint32_t *)out_feats, par,
-                                                               sidx, m, vpr, c2s);
-    } else {
-      int vpr = (int)(row_bytes / 2);
-      sub_feats_kernel<uint16_t><<<nblk(m * vpr), 256, 0, st>>>((const uint16_t *)feats, (uint16_t *)out_feats, par,
-                                                               sidx, m, vpr, c2s);
-    }
-    T2SC_LAUNCHED(ctx, "sub_feats");
-  }
   cudaFreeAsync(masks, st);
   cudaFreeAsync(counts, st);
   cudaFreeAsync(offs, st);
-  if (par != out_parent) cudaFreeAsync(par, st);
-  if (sidx != out_subidx) cudaFreeAsync(sidx, st);
   *m_out = m;
   return T2SC_OK;
 }
@@ -226,30 +229,12 @@ extern "C" int t2sc_subdivide_noalloc_device(t2sc_ctx *ctx, const int32_t *coord
     T2SC_LAUNCHED(ctx, "sub_count");
     r = scan_counts_into(ctx, counts, n, offs, offs + n, blocks);
     if (r != T2SC_OK) return r;
-    sub_emit_kernel<<<nblk(n), 256, 0, st>>>((const int4 *)coords, masks, offs, n, (int4 *)out_coords, out_parent,
-                                            out_subidx);
-    T2SC_LAUNCHED(ctx, "sub_emit");
+    r = emit_children(ctx, coords, masks, offs, n, feats, c, feats_mode, dtype, out_coords, out_feats, out_parent,
+                      out_subidx, err);
+    if (r != T2SC_OK) return r;
     int64_t mm = 0;
     T2SC_CUDA(cudaMemcpyAsync(&mm, offs + n, sizeof(int64_t), cudaMemcpyDeviceToHost, st), "subdivide count");
     T2SC_CUDA(cudaStreamSynchronize(st), "subdivide count");
-    if (feats_mode != T2SC_FEATS_NONE && mm > 0) {
-      const int64_t row_bytes = (int64_t)c * (dtype == T2SC_DT_F32 ? 4 : 2);
-      const int c2s = feats_mode == T2SC_FEATS_C2S;
-      if (row_bytes % 16 == 0) {
-        const int vpr = (int)(row_bytes / 16);
-        sub_feats_kernel<uint4><<<nblk(mm * vpr), 256, 0, st>>>((const uint4 *)feats, (uint4 *)out_feats, out_parent,
-                                                               out_subidx, mm, vpr, c2s);
-      } else if (row_bytes % 4 == 0) {
-        const int vpr = (int)(row_bytes / 4);
-        sub_feats_kernel<uint32_t><<<nblk(mm * vpr), 256, 0, st>>>((const uint32_t *)feats, (uint32_t *)out_feats,
-                                                                  out_parent, out_subidx, mm, vpr, c2s);
-      } else {
-        const int vpr = (int)(row_bytes / 2);
-        sub_feats_kernel<uint16_t><<<nblk(mm * vpr), 256, 0, st>>>((const uint16_t *)feats, (uint16_t *)out_feats,
-                                                                  out_parent, out_subidx, mm, vpr, c2s);
-      }
-      T2SC_LAUNCHED(ctx, "sub_feats");
-    }
     *m = mm;
     return T2SC_OK;
   }();
