@@ -709,10 +709,11 @@ def run_single(args):
 
 def run_distributed(args):
     """One rank per GPU (torchrun). cfg4 (the headline): the shell is cut
-    into z-slabs by the library (t2sc_partition_zslab); before every layer
-    each rank receives its one-voxel halo from its z-neighbours through the
-    library's own NCCL communicator (t2sc_halo_exchange_device), then
-    convolves (own + halo) rows with outputs for its own rows. Total work is
+    into z-slabs by the library (t2sc_partition_zslab); once per step each
+    rank receives a 4-plane halo from its z-neighbours through the library's
+    own NCCL communicator (t2sc_halo_exchange_device), then runs the four
+    layers on all its rows (own + halo): the halo rows' results are right
+    one plane less deep after every layer, the own rows after all four. Total work is
     fixed as N grows (strong scaling); `value` is the whole job's TFLOP/s
     over the slowest rank. cfg5 (extra keys): the four shapes are spread
     over the ranks (data parallel), and at N = 8 each shape is z-sharded
@@ -746,16 +747,21 @@ def run_distributed(args):
     # ------------------------------- cfg4 -------------------------------
     coords, x, ws, bs = inputs()
     comm = dist.Comm(ctx, ids[0], world, rank)
-    slab = dist.NativeSlab(coords, world, rank)
+    # a halo LAYERS planes deep, exchanged once per step: layer l is right on
+    # the own rows and the first LAYERS - l halo planes, so after the last
+    # layer the own rows equal the global chain (no exchange between layers)
+    slab = dist.NativeSlab(coords, world, rank, depth=LAYERS)
     rows, n_own = slab.rows, slab.n_own
     n_loc = len(rows)
     convs = [t2sc.SparseConv3d(w, b, dtype="bf16", ctx=ctx) for w, b in zip(ws, bs)]
-    c_all = t2sc.Coords(ctx, coords[rows], n_targets=n_own)
+    c_all = t2sc.Coords(ctx, coords[rows])  # every local row is a target
     torch.cuda.synchronize()
     t0 = time.perf_counter()
-    e_loc = c_all.build_map()
+    c_all.build_map()
     torch.cuda.synchronize()
     map_ms = 1e3 * (time.perf_counter() - t0)
+    # useful work = the edges of the own rows (the halo rows' convs are redundant)
+    e_loc = t2sc.Coords(ctx, coords[rows], n_targets=n_own).build_map()
     e_all = torch.tensor([e_loc], dtype=torch.int64, device="cuda")
     tdist.all_reduce(e_all)
     E = int(e_all.item())
@@ -765,8 +771,8 @@ def run_distributed(args):
 
     def step():
         cur = xin
+        comm.exchange(cur, slab.counts)  # the step input's deep halo
         for i, cv in enumerate(convs):
-            comm.exchange(cur, slab.counts)  # halo rows of this layer's input
             out = bufs[i & 1]
             conv_launch(L, _lib, ctx, cv, c_all.handle, cur, out)
             cur = out
@@ -855,7 +861,8 @@ def run_distributed(args):
                 "mvoxel_per_s": LAYERS * n / (ms * 1e-3) / 1e6, "map_build_ms": map_ms,
                 "config": {"workload": WORKLOAD, "voxels": n, "edges": E, "layers": LAYERS, "channels": C,
                            "l2": "flushed between steps (256 MiB write)",
-                           "parallelism": f"z-slab x{world}, one-voxel halo over the library's NCCL send/recv",
+                           "parallelism": f"z-slab x{world}, {LAYERS}-plane halo over the library's NCCL send/recv once per "
+                                          "step, every layer on own + halo rows",
                            "rank0_rows": n_own, "rank0_halo_rows": n_loc - n_own,
                            "cuda_graph": run is not step},
                 "e2e": {"value": flops / e2e_s / 1e12, "unit": UNIT, "h2d_bytes_per_step": n * C * 4,
@@ -897,7 +904,8 @@ def teardown(tdist, comm, rank):
 def run_cfg5_distributed(args, ctx, stream, flush, ids, rank, world):
     """cfg5 over `world` ranks: shapes round-robin when world <= 4, else
     groups of world // 4 ranks per shape with a z-slab split and a halo
-    exchange per layer on the group's own communicator."""
+    exchange of a two-plane halo per shape and step on the group's own
+    communicator."""
     import torch
     import torch.distributed as tdist
 
@@ -923,22 +931,26 @@ def run_cfg5_distributed(args, ctx, stream, flush, ids, rank, world):
         else:
             comm = dist.Comm(ctx, ids[1 + i], gs, rank % gs)
             comms.append(comm)
-            sl = dist.NativeSlab(coords, gs, rank % gs)
-            cd = t2sc.Coords(ctx, coords[sl.rows], n_targets=sl.n_own)
+            # a C5_LAYERS-plane halo exchanged once per shape and step; both
+            # layers run on own + halo rows (see the cfg4 split above)
+            sl = dist.NativeSlab(coords, gs, rank % gs, depth=C5_LAYERS)
+            cd = t2sc.Coords(ctx, coords[sl.rows])
             x = torch.zeros((len(sl.rows), C5), dtype=torch.bfloat16, device="cuda")
             x[:sl.n_own] = xg[torch.from_numpy(sl.own).cuda()]
             counts = sl.counts
-        e_loc += cd.build_map()
-        vox += cd.n
+        cd.build_map()
+        own = cd if gs == 1 else t2sc.Coords(ctx, coords[sl.rows], n_targets=sl.n_own)
+        e_loc += own.build_map()  # useful work: the own rows' edges
+        vox += cd.n if gs == 1 else sl.n_own
         bufs = [torch.zeros_like(x) for _ in range(2)]
         work.append((cd, x, bufs, comm, counts))
 
     def step5():
         for cd, x, bufs, comm, counts in work:
             cur = x
+            if comm is not None:
+                comm.exchange(cur, counts)
             for j, cv in enumerate(convs):
-                if comm is not None:
-                    comm.exchange(cur, counts)
                 conv_launch(L, _lib, ctx, cv, cd.handle, cur, bufs[j & 1])
                 cur = bufs[j & 1]
 

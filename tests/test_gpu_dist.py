@@ -40,3 +40,48 @@ def test_slabs_equal_global_conv(t2sc, world, dtype):
                                                   part.ctypes.data_as(ctypes.c_void_p), _lib.SILU, None), ctx.handle)
             y2[t0:t1] = part
         assert rel_err(y2, ref[sl.own]) <= (1e-6 if dtype == "f32" else F16_TOL)
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_deep_halo_four_layers_equal_global_chain(t2sc, world):
+    """One exchange of a 4-plane halo per 4-layer step: every layer runs on
+    all local rows (own + halo), each layer's results are right one plane
+    further in, so after four layers the own rows equal the global chain."""
+    import torch
+    from t2sc import _lib, dist
+    S = t2sc.synth
+    ctx = t2sc.Context.default(0)
+    ctx.set_stream(1)  # the legacy default stream: ordered with torch's default-stream work
+    try:
+        _deep_halo_case(t2sc, ctx, S, world)
+    finally:
+        ctx.set_stream(None)
+
+
+def _deep_halo_case(t2sc, ctx, S, world):
+    import torch
+    from t2sc import _lib, dist
+    coords = S.shell(*S.SHELLS["cfg1"])
+    n, c = len(coords), 64
+    x, _, _ = conv_inputs(S, n, c, c, seed=78)
+    layers = [conv_inputs(S, 1, c, c, seed=79 + i)[1:] for i in range(4)]
+    convs = [t2sc.SparseConv3d(w, b, dtype="bf16", ctx=ctx) for w, b in layers]
+
+    def chain(crd, xd):
+        cur = xd
+        for cv in convs:
+            out = torch.empty_like(cur)
+            _lib.check(_lib.lib.t2sc_conv_forward_device(cv.handle, crd.handle, ctypes.c_void_p(cur.data_ptr()),
+                                                         ctypes.c_void_p(out.data_ptr()), _lib.SILU, None),
+                       ctx.handle)
+            cur = out
+        torch.cuda.synchronize()
+        return cur.float().cpu().numpy()
+
+    xg = torch.from_numpy(x).cuda().to(torch.bfloat16)
+    ref = chain(t2sc.Coords(ctx, coords), xg)
+    for r in range(world):
+        sl = dist.NativeSlab(coords, world, r, depth=4)
+        xl = xg[torch.from_numpy(sl.rows).cuda()].contiguous()  # own rows + the exchanged 4-plane halo
+        y = chain(t2sc.Coords(ctx, coords[sl.rows]), xl)
+        assert rel_err(y[:sl.n_own], ref[sl.own]) <= F16_TOL
