@@ -64,3 +64,29 @@ def test_shape_then_texture_decoder_f32(t2sc, oracle):
     yt = tex.forward_guided(t2sc.SparseTensor(x, coords), subs)
     tc, ty, _ = oracle.decoder(sd_tex, CH, NB, coords, x, guide_subs=gsubs, pred_subdiv=False)
     assert np.array_equal(yt.coords, tc) and rel_err(yt.feats, ty) <= F32_TOL
+
+
+def test_decode_shape_and_tex(t2sc, oracle):
+    """decode_shape = forward + fdg_head (pipelines/image_to_3d.mojo:206-216),
+    decode_tex = forward_guided * 0.5 + 0.5 (:288-297), against the oracle's
+    decoder followed by its fdg_head."""
+    S = t2sc.synth
+    coords = S.shell(32, 10.0, 1.0)
+    x = S.normal(951, (len(coords), 8))
+    sd_shape = _state_dict(S, 8, 7, 1100)
+    dec = t2sc.SparseUnetVaeDecoder(sd_shape, CH, NB, pred_subdiv=True)
+    v, i, q, subs = t2sc.decode_shape(dec, t2sc.SparseTensor(x, coords), 0.5)
+    gsubs = [s.feats for s in subs]
+    oc, oy, _ = oracle.decoder(sd_shape, CH, NB, coords, x, guide_subs=gsubs, pred_subdiv=True)
+    ov, oi, oq = oracle.fdg_head(oy, 0.5)
+    assert np.array_equal(v.coords, oc)
+    # the heads are smooth in the decoder output except the > 0 threshold:
+    # compare intersected where the decoder outputs are not within the f32 bar of 0
+    assert rel_err(v.feats, ov) <= F32_TOL and rel_err(q.feats, oq) <= F32_TOL
+    clear = np.abs(oy[:, 3:6]) > 1e-3 * np.abs(oy).max()
+    assert np.array_equal(i.feats[clear], oi[clear])
+    sd_tex = _state_dict(S, 8, 6, 2100)
+    tex = t2sc.SparseUnetVaeDecoder(sd_tex, CH, NB, pred_subdiv=False)
+    yt = t2sc.decode_tex(tex, t2sc.SparseTensor(x, coords), subs)
+    _, ty, _ = oracle.decoder(sd_tex, CH, NB, coords, x, guide_subs=gsubs, pred_subdiv=False)
+    assert rel_err(yt.feats, ty * np.float32(0.5) + np.float32(0.5)) <= F32_TOL
