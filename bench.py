@@ -535,8 +535,7 @@ def extra_single(args, ctx, stream, flush):
                 "cfg5_mvoxel_per_s": C5_LAYERS * vox / (ms * 1e-3) / 1e6, "cfg5_frac": flops / (ms * 1e-3) / 1e12 / peak_tf,
                 "cfg5_workload": CFG5})
     del shapes
-    # ---- cfg2: one SubMConv3d(256->256) layer in f32 (split-TF32; also with
-    # f16-exact weights, two MMAs per k-step) and f16 ----
+    # ---- cfg2: one SubMConv3d(256->256) layer in f32 (split-TF32) and f16 ----
     S = t2sc.synth
     coords = S.shell(*S.SHELLS["cfg2"])
     n, c = len(coords), 256
@@ -547,10 +546,8 @@ def extra_single(args, ctx, stream, flush):
     g = torch.Generator(device="cuda").manual_seed(200)
     x32 = torch.randn((n, c), device="cuda", generator=g)
     f = 2.0 * e * c * c
-    w16 = w.astype(np.float16).astype(np.float32)  # an f16 checkpoint's weights
     for key, dt, wt, tdt, peak, label in (
             ("f32", "f32", w, torch.float32, peak_tf / 6, "TF32x3 = measured bf16 peak / 6"),
-            ("f32_f16w", "f32", w16, torch.float32, peak_tf / 4, "TF32x2 = measured bf16 peak / 4"),
             ("f16", "f16", w, torch.float16, peak_tf, "measured bf16 peak")):
         cv = t2sc.SparseConv3d(wt, b, dtype=dt, ctx=ctx)
         xin = x32.to(tdt)

@@ -124,11 +124,10 @@ int t2sc_csr_export(t2sc_coords *c, int kd, int kh, int kw, int dilation,
 /* ---- conv: weights uploaded once (replaces GpuSparseConv.try_build,
  * gpu/conv.mojo:264-329). weight is host f32 [Co, Kd, Kh, Kw, Ci] (the
  * conv_none layout), bias host f32 [Co] or NULL. Unlike try_build there is
- * no Co % 64 gate and no decline: every shape runs on the GPU. In
- * T2SC_DT_F32, weights that are all TF32-exact (the f16-exact weights that
- * the reference stores as f16, gpu/conv.mojo:32-36, always are) are found
- * at creation and run with two MMAs per k-step instead of three; the low
- * weight parts are then zero, so the result is that of the general path. ---- */
+ * no Co % 64 gate and no decline: every shape runs on the GPU. The
+ * reference's f16 weight storage (gpu/conv.mojo:32-36, chosen only when every
+ * weight is f16-exact) needs no mode here: such weights are passed as f32
+ * (exactly) and T2SC_DT_F32 gives the f32-storage result. ---- */
 int t2sc_conv_create(t2sc_ctx *ctx, const float *weight, const float *bias, int co, int kd,
                      int kh, int kw, int ci, int dilation, int dtype, t2sc_conv **out);
 int t2sc_conv_destroy(t2sc_conv *conv);

@@ -22,9 +22,8 @@ pytestmark = pytest.mark.gpu
 
 @pytest.mark.parametrize("dtype", ["f32", "f16", "f32_f16w"])
 def test_cfg2_residual_block(t2sc, oracle, dtype):
-    """f32_f16w: f32 activations with f16-exact weights (an f16 checkpoint,
-    gpu/conv.mojo:32-36), which the split-TF32 mode runs with two MMAs per
-    k-step instead of three."""
+    """f32_f16w: f32 activations with f16-exact weights, the reference's f16
+    checkpoint storage (gpu/conv.mojo:32-36), passed to the f32 mode."""
     S = t2sc.synth
     coords = S.shell(*S.SHELLS["cfg2"])
     n, c = len(coords), 256

@@ -96,10 +96,6 @@ struct TcArgs {
   int64_t n_pad;
   int ntiles, ci, co, bn, nchunks, nco_tiles, kvol, stages, flags, tmem_cols;
   uint32_t a_bytes, b_bytes, sub_bytes, stage_bytes;  // per (k, chunk) pair: A, B; pair slot; stage
-  // split-TF32 with TF32-exact weights (w_lo == 0): the x_hi*w_lo MMA and
-  // the w_lo copy are skipped; b_copy = the B bytes copied per pair
-  int w_exact;
-  uint32_t b_copy;
   int group;                                          // (k, chunk) pairs per pipeline stage
 #if T2SC_CONV_DIAGNOSTICS
   int debug;  // diagnostics (T2SC_CONV_DEBUG): 1 skips the gathers, 2 the MMAs, 4 the epilogue stores
@@ -344,7 +340,7 @@ __global__ void __launch_bounds__(Roles<DT, RB>::kThreads, 1)
         const int valid = npairs - q < a.group ? npairs - q : a.group;
         const uint32_t bar = full0 + 8 * s, abase = sbase + s * a.stage_bytes;
         if (lane == 0) T2SC_TRACE(8, it);
-        if (lane == 0) sm100::mbar_arrive_expect_tx(bar, T2SC_SKIP(8) ? 0u : (uint32_t)valid * a.b_copy);
+        if (lane == 0) sm100::mbar_arrive_expect_tx(bar, T2SC_SKIP(8) ? 0u : (uint32_t)valid * a.b_bytes);
         for (int g = 0; g < valid; g++, q++) {
           if (++c >= a.nchunks) {
             c = 0;
@@ -353,7 +349,7 @@ __global__ void __launch_bounds__(Roles<DT, RB>::kThreads, 1)
             wk = a.wimg + (size_t)((size_t)cot * a.kvol + k) * a.nchunks * a.b_bytes;
           }
           if (lane == 0 && !T2SC_SKIP(8))
-            sm100::bulk_g2s(abase + g * a.sub_bytes + a.a_bytes, wk + (size_t)c * a.b_bytes, a.b_copy, bar);
+            sm100::bulk_g2s(abase + g * a.sub_bytes + a.a_bytes, wk + (size_t)c * a.b_bytes, a.b_bytes, bar);
         }
         it++;
         if (++s == (uint32_t)S) {
@@ -514,7 +510,7 @@ __global__ void __launch_bounds__(Roles<DT, RB>::kThreads, 1)
                 } else if (kSplit) {
                   const uint64_t alo = ahi + (a_tile >> 4), blo = bhi + (b_tile >> 4);
                   sm100::mma_tf32_elect(dtm, alo, bhi, idesc, accum);
-                  if (!a.w_exact) sm100::mma_tf32_elect(dtm, ahi, blo, idesc, 1u);
+                  sm100::mma_tf32_elect(dtm, ahi, blo, idesc, 1u);
                   sm100::mma_tf32_elect(dtm, ahi, bhi, idesc, 1u);
                 } else {
                   sm100::mma_f16_elect(dtm, ahi, bhi, idesc, accum);
@@ -643,10 +639,6 @@ int conv_tc_prepare(t2sc_conv *cv, const float *w, std::string &err) {
   const size_t tile = (size_t)bn * cv->row_bytes, bbytes = tile * na;
   const size_t total = bbytes * cv->nco_tiles * K * cv->nchunks;
   std::vector<uint8_t> img(total, 0);
-  // TF32-exact weights (every f16 checkpoint's are: 10 mantissa bits and an
-  // exponent range inside f32's) have w_lo == 0, so the split-TF32 mode
-  // needs two MMAs per k-step instead of three, with the same result
-  bool lo_zero = f32;
   for (int nt = 0; nt < cv->nco_tiles; nt++)
     for (int k = 0; k < K; k++)
       for (int c = 0; c < cv->nchunks; c++) {
@@ -660,7 +652,6 @@ int conv_tc_prepare(t2sc_conv *cv, const float *w, std::string &err) {
               const float hi = tf32_round_host(v), lo = v - hi;
               memcpy(blk + off, &hi, 4);
               memcpy(blk + tile + off, &lo, 4);
-              if (lo != 0.0f) lo_zero = false;
             } else if (cv->dtype == T2SC_DT_BF16) {
               __nv_bfloat16 h = __float2bfloat16_rn(v);
               memcpy(blk + off, &h, 2);
@@ -670,7 +661,6 @@ int conv_tc_prepare(t2sc_conv *cv, const float *w, std::string &err) {
             }
           }
       }
-  cv->w_lo_zero = lo_zero;
   T2SC_CUDA(cudaMalloc(&cv->d_wtc, total), "conv weights");
   T2SC_CUDA(cudaMemcpy(cv->d_wtc, img.data(), total, cudaMemcpyHostToDevice), "conv weights upload");
   return T2SC_OK;
@@ -717,8 +707,6 @@ int conv_tc_launch(t2sc_conv *cv, t2sc_map *m, const void *x, void *y, int flags
   const int na = cv->dtype == T2SC_DT_F32 ? 2 : 1;
   a.a_bytes = kTileRows * cv->row_bytes * na;
   a.b_bytes = (uint32_t)cv->bn * cv->row_bytes * na;
-  a.w_exact = cv->w_lo_zero ? 1 : 0;
-  a.b_copy = cv->w_lo_zero ? (uint32_t)cv->bn * cv->row_bytes : a.b_bytes;
   a.sub_bytes = (a.a_bytes + a.b_bytes + 1023u) & ~1023u;
   const int idx_bytes = 2 * kMaxK * kTileRows * 4;  // double-buffered tile index blocks
   // CTAs per SM: 2 independent pipelines when both fit (TMEM <= 256 columns

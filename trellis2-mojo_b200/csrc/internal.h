@@ -90,7 +90,6 @@ struct t2sc_conv {
   int tc_path = 0;               // 1 = tcgen05 path, 0 = SIMT path
   float *d_w_simt = nullptr;     // [K][ci][co] f32 (SIMT path)
   void *d_w_lo = nullptr;        // split-TF32 low parts image (f32 mode)
-  bool w_lo_zero = false;        // f32 mode: every weight is TF32-exact (w_lo == 0)
 };
 
 namespace t2sc {
