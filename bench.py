@@ -800,10 +800,16 @@ def run_distributed(args):
     launches0 = ctx.launch_count()
     clk = Clocks(local).__enter__() if rank == 0 else None
     time.sleep(0.3)
+    tok = torch.zeros(1, device="cuda")
     for _ in range(args.steps):
         flush.zero_()
         torch.cuda.synchronize()
         tdist.barrier()
+        # the host barrier releases the ranks microseconds to ~0.1 ms apart; a
+        # one-element all-reduce ordered before the start event aligns them
+        # on the device, so that no rank's timed step includes waiting for a
+        # peer that has not launched yet
+        tdist.all_reduce(tok)
         s0, s1 = ev(), ev()
         s0.record(stream)
         run()
@@ -876,7 +882,7 @@ def teardown(tdist, comm, rank):
     """Ends a distributed run: the library's communicator is finalised and
     destroyed (bounded inside the library), then torch's process group. Its
     teardown has blocked at exit on this pool after the run's work was done,
-    so a watchdog ends the process 30 s after the results were printed if it
+    so a watchdog ends the process 10 s after the results were printed if it
     does not return; each step is logged to stderr with its time."""
     import threading
 
@@ -886,8 +892,8 @@ def teardown(tdist, comm, rank):
         print(f"# rank {rank} teardown +{time.perf_counter() - t0:.2f}s: {msg}", file=sys.stderr, flush=True)
 
     def watchdog():
-        time.sleep(30)
-        log("process-group teardown did not return within 30 s; exiting")
+        time.sleep(10)
+        log("process-group teardown did not return within 10 s; exiting")
         os._exit(0)
 
     threading.Thread(target=watchdog, daemon=True).start()
@@ -954,11 +960,13 @@ def run_cfg5_distributed(args, ctx, stream, flush, ids, rank, world):
     for _ in range(args.warmup):
         step5()
     torch.cuda.synchronize()
+    tok = torch.zeros(1, device="cuda")
     times = []
     for _ in range(args.steps):
         flush.zero_()
         torch.cuda.synchronize()
         tdist.barrier()
+        tdist.all_reduce(tok)  # device-side alignment of the ranks (as for cfg4)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
         step5()
