@@ -163,6 +163,24 @@ class SparseTensor:
         # reference's ArcPointer spatial cache
         self._cache = _cache if _cache is not None else {}
 
+    def seqlen(self, b):
+        """Rows of batch b (basic.mojo:378-379)."""
+        return int(self.offsets[b + 1] - self.offsets[b])
+
+    def seqlen_list(self):
+        return [self.seqlen(b) for b in range(self.batch_size)]
+
+    def batch_broadcast_map(self):
+        """Row index -> batch index (basic.mojo:149-155, 384-385)."""
+        return np.repeat(np.arange(self.batch_size), np.diff(self.offsets)).tolist()
+
+    def spatial_shape(self):
+        """Per spatial axis, the largest coordinate + 1, cached with the
+        coordinates like the reference's "shape" entry (basic.mojo:387-395)."""
+        if "shape" not in self._cache:
+            self._cache["shape"] = [int(self.coords[:, c].max()) + 1 if len(self.coords) else 0 for c in (1, 2, 3)]
+        return list(self._cache["shape"])
+
     @property
     def ctx(self):
         if self._ctx is None:
