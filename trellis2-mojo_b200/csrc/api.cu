@@ -2,6 +2,7 @@
 #include <stdio.h>
 #include <stdlib.h>
 
+#include <algorithm>
 #include <new>
 #include <vector>
 
@@ -132,6 +133,8 @@ int t2sc_ctx_destroy(t2sc_ctx *ctx) {
   for (auto &kv : ctx->id_maps) free_map(kv.second);
   cudaFree(ctx->d_err);
   if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
+  if (ctx->up_stream) cudaStreamDestroy(ctx->up_stream);
+  if (ctx->down_stream) cudaStreamDestroy(ctx->down_stream);
   delete ctx;
   return T2SC_OK;
 }
@@ -211,6 +214,11 @@ int t2sc_coords_destroy(t2sc_coords *c) {
   // stream-ordered release: work already queued on the context's stream
   // that reads these buffers still runs first, and nothing synchronises
   for (auto &kv : c->maps) free_map(kv.second);
+  for (auto &kv : c->chain_plans)
+    for (auto &sl : kv.second) {
+      t2sc_coords_destroy(sl.all);
+      t2sc_coords_destroy(sl.own);
+    }
   cudaFreeAsync(c->d_coords, c->ctx->stream);
   cudaFreeAsync(c->d_slots, c->ctx->stream);
   delete c;
@@ -435,6 +443,200 @@ int t2sc_conv_forward(t2sc_conv *cv, t2sc_coords *c, const float *x, float *y, i
   });
 }
 
+}  // extern "C"
+
+// ---------------------------- pipelined chain -----------------------------
+//
+// A chain over host buffers is bound by the PCIe copies of its input and
+// output (f32, both ways), not by the convs. When the rows are ordered by
+// (batch, x), as coordinate sets built in lexicographic order are, the rows
+// split into contiguous slabs along x; each slab is run on its own rows
+// plus a halo as deep as the chain's reach along x, so that its own rows'
+// outputs equal the whole set's (a halo row's layer-i result is right while
+// its depth is within the reach still left after layer i). Slab uploads,
+// slab chains and slab downloads run on three streams, so the upload of
+// slab s + 1 and the download of slab s - 1 overlap the convs of slab s and
+// each other (host-to-device and device-to-host copies run concurrently).
+
+constexpr int64_t kChainMinRows = 200000;   // smaller sets run unsplit
+constexpr int64_t kChainRowsPerSlab = 100000;
+constexpr int kChainMaxSlabs = 8;
+
+// Slab plan of a coordinate set for a reach (cached on the set; an empty
+// plan means the set runs unsplit: too small, not ordered by (batch, x), or
+// halos too large to pay off). Building it reads the coordinates back once.
+static int chain_plan(t2sc_coords *c, int64_t reach, const std::vector<t2sc_chain_slab> **out) {
+  t2sc_ctx *ctx = c->ctx;
+  std::string &err = ctx->last_error;
+  auto it = c->chain_plans.find(reach);
+  if (it != c->chain_plans.end()) {
+    *out = &it->second;
+    return T2SC_OK;
+  }
+  std::vector<t2sc_chain_slab> plan;
+  const int64_t n = c->n;
+  const int nslab = (int)std::min<int64_t>(kChainMaxSlabs, n / kChainRowsPerSlab);
+  if (n >= kChainMinRows && nslab >= 2) {
+    std::vector<int32_t> h((size_t)n * 4);
+    T2SC_CUDA(cudaMemcpyAsync(h.data(), c->d_coords, (size_t)n * 16, cudaMemcpyDeviceToHost, ctx->stream),
+              "chain plan");
+    T2SC_CUDA(cudaStreamSynchronize(ctx->stream), "chain plan");
+    std::vector<int64_t> key((size_t)n);
+    bool sorted = true;
+    for (int64_t r = 0; r < n; r++) {
+      key[r] = (int64_t)h[4 * r] * (int64_t(1) << 22) + (h[4 * r + 1] + (int64_t(1) << 20));
+      if (r > 0 && key[r] < key[r - 1]) {
+        sorted = false;
+        break;
+      }
+    }
+    if (sorted) {
+      // own ranges cut where the (batch, x) key changes, near n * s / nslab
+      std::vector<int64_t> cut{0};
+      for (int s = 1; s < nslab; s++) {
+        int64_t r = std::max(cut.back() + 1, n * s / nslab);
+        while (r < n && key[r] == key[r - 1]) r++;
+        if (r < n) cut.push_back(r);
+      }
+      cut.push_back(n);
+      int64_t local_max = 0, local_sum = 0;
+      for (size_t s = 0; s + 1 < cut.size(); s++) {
+        t2sc_chain_slab sl;
+        sl.t0 = cut[s];
+        sl.t1 = cut[s + 1];
+        sl.lo = std::lower_bound(key.begin(), key.end(), key[sl.t0] - reach) - key.begin();
+        sl.hi = std::upper_bound(key.begin(), key.end(), key[sl.t1 - 1] + reach) - key.begin();
+        local_max = std::max(local_max, sl.hi - sl.lo);
+        local_sum += sl.hi - sl.lo;
+        plan.push_back(sl);
+      }
+      // worth it only if the halos stay small next to the own rows
+      if (plan.size() < 2 || local_sum > n + n / 3 || local_max > n / 2) plan.clear();
+      for (auto &sl : plan) {
+        int rc = coords_create_impl(ctx, c->d_coords + 4 * sl.lo, sl.hi - sl.lo, sl.hi - sl.lo, true, &sl.all);
+        if (rc == T2SC_OK)
+          rc = coords_create_impl(ctx, c->d_coords + 4 * sl.lo, sl.hi - sl.lo, sl.t1 - sl.t0, true, &sl.own,
+                                  sl.t0 - sl.lo);
+        if (rc != T2SC_OK) {
+          for (auto &q : plan) {
+            t2sc_coords_destroy(q.all);
+            t2sc_coords_destroy(q.own);
+          }
+          return rc;
+        }
+      }
+    }
+  }
+  auto ins = c->chain_plans.emplace(reach, std::move(plan));
+  *out = &ins.first->second;
+  return T2SC_OK;
+}
+
+// Runs `body` with the context's stream set to `st` (the conversion helpers
+// and the conv launches issue on the context's stream).
+template <class F>
+static int on_stream(t2sc_ctx *ctx, cudaStream_t st, F &&body) {
+  cudaStream_t prev = ctx->stream;
+  ctx->stream = st;
+  int rc = body();
+  ctx->stream = prev;
+  return rc;
+}
+
+static int chain_pipelined(t2sc_conv *const *convs, int n_layers, t2sc_coords *c,
+                           const std::vector<t2sc_chain_slab> &plan, const float *x, float *y, const int *flags,
+                           int cmax) {
+  t2sc_ctx *ctx = c->ctx;
+  std::string &err = ctx->last_error;
+  const int dtype = convs[0]->dtype;
+  const size_t es = elem_size(dtype);
+  const int64_t n = c->n, ci = convs[0]->ci, co = convs[n_layers - 1]->co;
+  if (!ctx->up_stream) T2SC_CUDA(cudaStreamCreateWithFlags(&ctx->up_stream, cudaStreamNonBlocking), "chain stream");
+  if (!ctx->down_stream)
+    T2SC_CUDA(cudaStreamCreateWithFlags(&ctx->down_stream, cudaStreamNonBlocking), "chain stream");
+  cudaStream_t cs = ctx->stream, up = ctx->up_stream, dn = ctx->down_stream;
+  int64_t local_max = 0;
+  for (auto &sl : plan) local_max = std::max(local_max, sl.hi - sl.lo);
+  DevBuf din, dout, stage_in, stage_out, b0, b1;
+  const bool f32 = dtype == T2SC_DT_F32;
+  T2SC_TRY(din.alloc(ctx, n * ci * es));
+  T2SC_TRY(dout.alloc(ctx, n * co * es));
+  if (!f32) {
+    T2SC_TRY(stage_in.alloc(ctx, n * ci * 4));
+    T2SC_TRY(stage_out.alloc(ctx, n * co * 4));
+  }
+  T2SC_TRY(b0.alloc(ctx, local_max * cmax * es));
+  T2SC_TRY(b1.alloc(ctx, local_max * cmax * es));
+  const size_t ns = plan.size();
+  std::vector<cudaEvent_t> ev(2 * ns + 2, nullptr);
+  for (auto &e : ev) T2SC_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "chain event");
+  struct EventsGuard {
+    std::vector<cudaEvent_t> &v;
+    ~EventsGuard() {
+      for (auto e : v)
+        if (e) cudaEventDestroy(e);
+    }
+  } guard_ev{ev};
+  cudaEvent_t ev_start = ev[2 * ns], ev_end = ev[2 * ns + 1];
+  // the copy streams start after the allocations (and earlier work) on the context's stream
+  T2SC_CUDA(cudaEventRecord(ev_start, cs), "chain event");
+  T2SC_CUDA(cudaStreamWaitEvent(up, ev_start, 0), "chain event");
+  T2SC_CUDA(cudaStreamWaitEvent(dn, ev_start, 0), "chain event");
+  uint8_t *din8 = (uint8_t *)din.p, *dout8 = (uint8_t *)dout.p;
+  int64_t uploaded = 0;
+  for (size_t s = 0; s < ns; s++) {
+    const t2sc_chain_slab &sl = plan[s];
+    // upload: rows [uploaded, hi) (the part of this slab's rows not yet on the device)
+    const int64_t r1 = s + 1 == ns ? n : sl.hi;
+    if (r1 > uploaded) {
+      const int64_t cnt = (r1 - uploaded) * ci;
+      if (f32) {
+        T2SC_CUDA(cudaMemcpyAsync(din8 + uploaded * ci * 4, x + uploaded * ci, cnt * 4, cudaMemcpyHostToDevice, up),
+                  "chain upload");
+      } else {
+        float *st = (float *)stage_in.p + uploaded * ci;
+        T2SC_CUDA(cudaMemcpyAsync(st, x + uploaded * ci, cnt * 4, cudaMemcpyHostToDevice, up), "chain upload");
+        T2SC_TRY(on_stream(ctx, up, [&] { return f32_to_dtype(ctx, st, din8 + uploaded * ci * es, cnt, dtype); }));
+      }
+      uploaded = r1;
+    }
+    T2SC_CUDA(cudaEventRecord(ev[s], up), "chain event");
+    // the slab's chain on the context's stream
+    T2SC_CUDA(cudaStreamWaitEvent(cs, ev[s], 0), "chain event");
+    const void *cur = din8 + sl.lo * ci * es;
+    void *bufs[2] = {b0.p, b1.p};
+    for (int i = 0; i < n_layers; i++) {
+      const int f = flags ? flags[i] : 0;
+      const bool last = i == n_layers - 1;
+      t2sc_coords *h = last ? sl.own : sl.all;
+      void *outp = last ? (void *)(dout8 + sl.t0 * co * es) : bufs[i & 1];
+      const void *res = (f & T2SC_RESIDUAL) ? (const void *)(din8 + (last ? sl.t0 : sl.lo) * ci * es) : nullptr;
+      T2SC_TRY(forward_device_impl(convs[i], h, cur, outp, f, res));
+      cur = outp;
+    }
+    T2SC_CUDA(cudaEventRecord(ev[ns + s], cs), "chain event");
+    // download the own rows
+    T2SC_CUDA(cudaStreamWaitEvent(dn, ev[ns + s], 0), "chain event");
+    const int64_t cnt = (sl.t1 - sl.t0) * co;
+    if (f32) {
+      T2SC_CUDA(cudaMemcpyAsync(y + sl.t0 * co, dout8 + sl.t0 * co * 4, cnt * 4, cudaMemcpyDeviceToHost, dn),
+                "chain download");
+    } else {
+      float *st = (float *)stage_out.p + sl.t0 * co;
+      T2SC_TRY(on_stream(ctx, dn, [&] { return dtype_to_f32(ctx, dout8 + sl.t0 * co * es, st, cnt, dtype); }));
+      T2SC_CUDA(cudaMemcpyAsync(y + sl.t0 * co, st, cnt * 4, cudaMemcpyDeviceToHost, dn), "chain download");
+    }
+  }
+  // the context's stream waits for the last download (buffers are freed on it)
+  T2SC_CUDA(cudaEventRecord(ev_end, dn), "chain event");
+  T2SC_CUDA(cudaStreamWaitEvent(cs, ev_end, 0), "chain event");
+  T2SC_CUDA(cudaEventRecord(ev_end, up), "chain event");
+  T2SC_CUDA(cudaStreamWaitEvent(cs, ev_end, 0), "chain event");
+  return check_sync(ctx);
+}
+
+extern "C" {
+
 int t2sc_conv_chain_forward(t2sc_conv *const *convs, int n_layers, t2sc_coords *c, const float *x, float *y,
                             const int *flags) {
   if (!convs || n_layers <= 0 || !c || !convs[0]) return T2SC_ERR_INVALID;
@@ -458,6 +660,11 @@ int t2sc_conv_chain_forward(t2sc_conv *const *convs, int n_layers, t2sc_coords *
       return fail(ctx, T2SC_ERR_INVALID, "chain: coordinates with halo rows are not chainable");
     if (n == 0) return T2SC_OK;
     if (!x || !y) return fail(ctx, T2SC_ERR_INVALID, "null feature buffer");
+    int64_t reach = 0;  // rows a chain output depends on lie within this many x planes
+    for (int i = 0; i < n_layers; i++) reach += (int64_t)(convs[i]->kd / 2) * convs[i]->dilation;
+    const std::vector<t2sc_chain_slab> *plan = nullptr;
+    T2SC_TRY(chain_plan(c, reach, &plan));
+    if (!plan->empty()) return chain_pipelined(convs, n_layers, c, *plan, x, y, flags, cmax);
     DevBuf din, b0, b1;
     T2SC_TRY(upload_as(ctx, x, n * convs[0]->ci, dtype, din));
     T2SC_TRY(b0.alloc(ctx, n * cmax * elem_size(dtype)));

@@ -47,6 +47,8 @@ struct t2sc_ctx {
   // grow-only scratch buffers ([0]: the split-TF32 hi/lo parts of a conv input)
   void *stage[4] = {nullptr, nullptr, nullptr, nullptr};
   size_t stage_cap[4] = {0, 0, 0, 0};
+  // copy streams of the pipelined conv chain (created on first use)
+  cudaStream_t up_stream = nullptr, down_stream = nullptr;
 };
 
 // One neighbour map for a (kernel, dilation) on a coordinate set. Device
@@ -65,6 +67,15 @@ struct t2sc_map {
   uint32_t *tile_mask = nullptr; // [ntiles]  OR of masks in each 128-row tile
 };
 
+// One row slab of a pipelined conv chain (api.cu): local rows [lo, hi) of
+// the parent coordinate set (own rows [t0, t1) plus a halo as deep as the
+// chain's reach along x), a handle whose targets are all local rows and one
+// whose targets are the own rows.
+struct t2sc_chain_slab {
+  int64_t lo = 0, t0 = 0, t1 = 0, hi = 0;
+  t2sc_coords *all = nullptr, *own = nullptr;
+};
+
 struct t2sc_coords {
   t2sc_ctx *ctx = nullptr;
   int64_t n = 0;                 // all rows (targets first, then halo rows)
@@ -76,6 +87,8 @@ struct t2sc_coords {
   // probe reads key and row with one load)
   longlong2 *d_slots = nullptr;
   std::map<std::tuple<int, int, int, int>, t2sc_map *> maps;
+  // pipelined-chain plans per x-reach (empty: this set is not pipelined)
+  std::map<int64_t, std::vector<t2sc_chain_slab>> chain_plans;
 };
 
 struct t2sc_conv {
