@@ -145,7 +145,13 @@ int t2sc_conv_forward_device(t2sc_conv *conv, t2sc_coords *coords, const void *x
 /* A chain of convs on the same coordinates with device-resident
  * intermediates: host f32 x [N, Ci0] in, host f32 y [N, Co_last] out.
  * flags[i] applies to layer i; T2SC_RESIDUAL on layer i adds the chain input
- * x (the identity residual of a residual block). All convs share one dtype. */
+ * x (the identity residual of a residual block). All convs share one dtype.
+ * A set of >= 200k rows ordered by (batch, x) runs as x-slabs, each with a
+ * halo as deep as the chain's reach along x, with slab uploads, convs and
+ * downloads overlapped on the context's stream and two copy streams; the
+ * results equal one unsplit pass. The slab plan (two coordinate handles
+ * and maps per slab) is built on the first such call for a coordinate set
+ * and kept with it; building it reads the coordinates back once. */
 int t2sc_conv_chain_forward(t2sc_conv *const *convs, int n_layers, t2sc_coords *coords,
                             const float *x, float *y, const int *flags);
 
