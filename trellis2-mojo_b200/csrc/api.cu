@@ -532,17 +532,6 @@ static int chain_plan(t2sc_coords *c, int64_t reach, const std::vector<t2sc_chai
   return T2SC_OK;
 }
 
-// Runs `body` with the context's stream set to `st` (the conversion helpers
-// and the conv launches issue on the context's stream).
-template <class F>
-static int on_stream(t2sc_ctx *ctx, cudaStream_t st, F &&body) {
-  cudaStream_t prev = ctx->stream;
-  ctx->stream = st;
-  int rc = body();
-  ctx->stream = prev;
-  return rc;
-}
-
 static int chain_pipelined(t2sc_conv *const *convs, int n_layers, t2sc_coords *c,
                            const std::vector<t2sc_chain_slab> &plan, const float *x, float *y, const int *flags,
                            int cmax) {
@@ -583,26 +572,25 @@ static int chain_pipelined(t2sc_conv *const *convs, int n_layers, t2sc_coords *c
   T2SC_CUDA(cudaStreamWaitEvent(up, ev_start, 0), "chain event");
   T2SC_CUDA(cudaStreamWaitEvent(dn, ev_start, 0), "chain event");
   uint8_t *din8 = (uint8_t *)din.p, *dout8 = (uint8_t *)dout.p;
+  // The copy streams carry only copies (back to back, so the copy engines
+  // never wait for a conversion kernel); conversions run on the context's
+  // stream with the convs.
   int64_t uploaded = 0;
   for (size_t s = 0; s < ns; s++) {
     const t2sc_chain_slab &sl = plan[s];
     // upload: rows [uploaded, hi) (the part of this slab's rows not yet on the device)
-    const int64_t r1 = s + 1 == ns ? n : sl.hi;
-    if (r1 > uploaded) {
-      const int64_t cnt = (r1 - uploaded) * ci;
-      if (f32) {
-        T2SC_CUDA(cudaMemcpyAsync(din8 + uploaded * ci * 4, x + uploaded * ci, cnt * 4, cudaMemcpyHostToDevice, up),
-                  "chain upload");
-      } else {
-        float *st = (float *)stage_in.p + uploaded * ci;
-        T2SC_CUDA(cudaMemcpyAsync(st, x + uploaded * ci, cnt * 4, cudaMemcpyHostToDevice, up), "chain upload");
-        T2SC_TRY(on_stream(ctx, up, [&] { return f32_to_dtype(ctx, st, din8 + uploaded * ci * es, cnt, dtype); }));
-      }
+    const int64_t r0 = uploaded, r1 = s + 1 == ns ? n : sl.hi;
+    if (r1 > r0) {
+      const int64_t cnt = (r1 - r0) * ci;
+      void *dst = f32 ? (void *)(din8 + r0 * ci * 4) : (void *)((float *)stage_in.p + r0 * ci);
+      T2SC_CUDA(cudaMemcpyAsync(dst, x + r0 * ci, cnt * 4, cudaMemcpyHostToDevice, up), "chain upload");
       uploaded = r1;
     }
     T2SC_CUDA(cudaEventRecord(ev[s], up), "chain event");
     // the slab's chain on the context's stream
     T2SC_CUDA(cudaStreamWaitEvent(cs, ev[s], 0), "chain event");
+    if (!f32 && r1 > r0)
+      T2SC_TRY(f32_to_dtype(ctx, (const float *)stage_in.p + r0 * ci, din8 + r0 * ci * es, (r1 - r0) * ci, dtype));
     const void *cur = din8 + sl.lo * ci * es;
     void *bufs[2] = {b0.p, b1.p};
     for (int i = 0; i < n_layers; i++) {
@@ -614,18 +602,13 @@ static int chain_pipelined(t2sc_conv *const *convs, int n_layers, t2sc_coords *c
       T2SC_TRY(forward_device_impl(convs[i], h, cur, outp, f, res));
       cur = outp;
     }
+    const int64_t cnt = (sl.t1 - sl.t0) * co;
+    const float *src = f32 ? (const float *)(dout8 + sl.t0 * co * 4) : (const float *)stage_out.p + sl.t0 * co;
+    if (!f32) T2SC_TRY(dtype_to_f32(ctx, dout8 + sl.t0 * co * es, (float *)src, cnt, dtype));
     T2SC_CUDA(cudaEventRecord(ev[ns + s], cs), "chain event");
     // download the own rows
     T2SC_CUDA(cudaStreamWaitEvent(dn, ev[ns + s], 0), "chain event");
-    const int64_t cnt = (sl.t1 - sl.t0) * co;
-    if (f32) {
-      T2SC_CUDA(cudaMemcpyAsync(y + sl.t0 * co, dout8 + sl.t0 * co * 4, cnt * 4, cudaMemcpyDeviceToHost, dn),
-                "chain download");
-    } else {
-      float *st = (float *)stage_out.p + sl.t0 * co;
-      T2SC_TRY(on_stream(ctx, dn, [&] { return dtype_to_f32(ctx, dout8 + sl.t0 * co * es, st, cnt, dtype); }));
-      T2SC_CUDA(cudaMemcpyAsync(y + sl.t0 * co, st, cnt * 4, cudaMemcpyDeviceToHost, dn), "chain download");
-    }
+    T2SC_CUDA(cudaMemcpyAsync(y + sl.t0 * co, src, cnt * 4, cudaMemcpyDeviceToHost, dn), "chain download");
   }
   // the context's stream waits for the last download (buffers are freed on it)
   T2SC_CUDA(cudaEventRecord(ev_end, dn), "chain event");
